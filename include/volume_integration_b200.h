@@ -1,0 +1,137 @@
+/*
+ * C ABI of the B200 volume-integration renderer (libvi_b200.so).
+ *
+ * Plain pointers and sizes only; every pointer argument is CUDA device memory
+ * unless stated otherwise, and every call is asynchronous on `stream` (a
+ * cudaStream_t; NULL = legacy default stream) except where noted.  Each entry
+ * point returns a vi_status code; vi_last_error() gives a message for the
+ * calling thread's last failure.
+ *
+ * The entry points replace the reference extension's pybind functions
+ * (reference: ext.cpp:18-20, integrate_primitives.h:42-139) one for one, with
+ * the same argument order and meaning; a torch binding with the reference's
+ * exact Python signature sits on top of them (volume_integration._C).
+ */
+#ifndef VOLUME_INTEGRATION_B200_H
+#define VOLUME_INTEGRATION_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum vi_status {
+  VI_OK = 0,
+  VI_ERR_INVALID_ARGUMENT = 1, /* a size or pointer is inconsistent */
+  VI_ERR_UNSUPPORTED = 2,      /* a configuration outside what the kernels implement */
+  VI_ERR_ALLOC = 3,            /* a state-buffer callback returned NULL */
+  VI_ERR_CUDA = 4,             /* a CUDA runtime call failed */
+  VI_ERR_TOO_MANY_OVERLAPS = 5,/* more than 2^30 tile/primitive overlaps */
+  VI_ERR_DEVICE = 6            /* a kernel latched an error in the state's status word */
+} vi_status;
+
+/* Grows the caller's byte buffer to at least nbytes and returns its device
+ * address (reference: resizeFunctional, integrate_primitives.cu:54-68). */
+typedef char* (*vi_resize_fn)(void* user, size_t nbytes);
+
+/* Message for the calling thread's last non-VI_OK return. */
+const char* vi_last_error(void);
+
+/*
+ * Forward pass.  Replaces IntegratePrimitivesCUDA
+ * (reference: integrate_primitives.h:42-82, integrate_primitives.cu:74-287) and
+ * Integrator::forward (cuda_integrator/integrator_impl.cu:196-469).
+ *
+ * Outputs (caller-allocated, overwritten): out_color [3,H,W], out_features
+ * [output_feature_dim,H,W], visibility_info [H,W] (float32, CHW), and
+ * *num_rendered (host int).  The three state buffers are obtained through the
+ * callbacks and must be passed unchanged to the backward.  Inputs follow the
+ * reference's positional order; resolution/do_hash hold hashgrid_levels
+ * entries, primes 3, viewmatrix/projmatrix 16 column-major floats, bg_color 3.
+ * Blocks the host once, to read the overlap count.
+ */
+int vi_integrate_primitives(
+    vi_resize_fn geom_buffer, void* geom_user, vi_resize_fn binning_buffer, void* binning_user,
+    vi_resize_fn img_buffer, void* img_user, float* out_color, float* out_features, float* visibility_info,
+    int* num_rendered, int P, const float* means3D, const float* primitive_confidences, float primitive_scale,
+    const float* viewmatrix, const float* projmatrix, const float* cam_pos, float tan_fovx, float tan_fovy,
+    int image_height, int image_width, float near_plane, float max_distance, const float* feature_table,
+    uint64_t feature_table_numel, const int* resolution, const int* do_hash, const int* primes, int feature_offset,
+    const float* linear_weights, uint64_t linear_weights_numel, const float* linear_bias,
+    uint64_t linear_bias_numel, int stencil_genus, int grid_size, int max_primitives_per_ray,
+    float occupancy_threshold, const float* bg_color, unsigned input_feature_dim, unsigned output_feature_dim,
+    unsigned intermediate_feature_dim, unsigned hashgrid_levels, unsigned num_output_channels, int debug,
+    void* stream);
+
+/*
+ * Backward pass.  Replaces IntegratePrimitivesBackwardCUDA
+ * (reference: integrate_primitives.h:86-133, integrate_primitives.cu:294-432) and
+ * Integrator::backward (cuda_integrator/integrator_impl.cu:474-756).
+ *
+ * Gradient outputs (caller-allocated, overwritten): dL_dmeans3D [P,3] (zeros,
+ * as in the reference), dL_dconfidences [P,G^3], dL_dfeature_table
+ * [feature_table_size], dL_dlinear_weights [O*D], dL_dlinear_bias [O] with
+ * D = hashgrid_levels*input_feature_dim, O = 3 + output_feature_dim + 1.
+ * geom/binning/img are the device addresses of the forward's state buffers.
+ */
+int vi_integrate_primitives_backward(
+    float* dL_dmeans3D, float* dL_dconfidences, float* dL_dfeature_table, float* dL_dlinear_weights,
+    float* dL_dlinear_bias, const float* dL_dout_color, const float* dL_dout_features, char* geom_buffer,
+    char* binning_buffer, char* img_buffer, const float* means3D, const float* primitive_confidences,
+    float primitive_scale, const float* viewmatrix, const float* projmatrix, const float* cam_pos, float tan_fovx,
+    float tan_fovy, int image_height, int image_width, float near_plane, float max_distance,
+    const float* feature_table, const int* resolution, const int* do_hash, const int* primes, int feature_offset,
+    const float* linear_weights, const float* linear_bias, int stencil_genus, int grid_size,
+    int max_primitives_per_ray, float occupancy_threshold, const float* bg_color, unsigned input_feature_dim,
+    unsigned output_feature_dim, unsigned hashgrid_levels, unsigned num_output_channels,
+    uint64_t feature_table_size, int P, int num_rendered, int debug, void* stream);
+
+/* Frustum test per primitive (view-space z > 0.2).  Replaces markVisible
+ * (reference: integrate_primitives.h:136-139, integrate_primitives.cu:436-462). */
+int vi_mark_visible(int P, const float* means3D, const float* viewmatrix, const float* projmatrix, uint8_t* present,
+                    void* stream);
+
+/*
+ * Stable radix sort of (uint64 key, uint32 value) pairs over key bits
+ * [begin_bit, end_bit): the sort the reference binning step takes from
+ * cub::DeviceRadixSort::SortPairs (reference:
+ * cuda_integrator/integrator_impl.cu:341-349).  temp must hold
+ * vi_sort_pairs_temp_bytes(n, begin_bit, end_bit) bytes; keys_in/vals_in are
+ * used as scratch and are clobbered.  n < 2^30.
+ */
+size_t vi_sort_pairs_temp_bytes(uint64_t n, int begin_bit, int end_bit);
+int vi_sort_pairs(uint64_t* keys_in, uint32_t* vals_in, uint64_t* keys_out, uint32_t* vals_out, uint64_t n,
+                  int begin_bit, int end_bit, void* temp, size_t temp_bytes, void* stream);
+
+/* Number of key bits the reference sorts on: 32 + getHigherMsb(tiles)
+ * (reference: cuda_integrator/integrator_impl.cu:47-62, :341). */
+int vi_sort_end_bit(uint32_t num_tiles);
+
+/*
+ * Byte offsets of the integer state inside the forward's buffers, so callers
+ * (and parity tests) can read radii, the sorted point list, tile ranges and the
+ * per-pixel contributor lists in the reference's formats
+ * (reference: cuda_integrator/integrator_impl.h:35-146).
+ */
+typedef struct vi_state_layout {
+  size_t geom_bytes, binning_bytes, img_bytes;
+  /* geometry buffer */
+  size_t status, depths, radii, means2D, tiles_touched, rec_cnt, rec_key, rec_props;
+  int props_stride;
+  /* binning buffer: sorted tile ids and primitive ids (the point list) */
+  size_t sorted_tiles, point_list;
+  /* image buffer */
+  size_t ranges, final_T, n_contrib, contrib_idx, delta_t, contrib_rec;
+} vi_state_layout;
+int vi_get_state_layout(int P, int64_t num_rendered, int image_height, int image_width, int max_primitives_per_ray,
+                        int grid_size, unsigned output_feature_dim, vi_state_layout* out);
+
+/* Reads the status word a forward latched in its geometry buffer (blocks). */
+int vi_read_device_status(const char* geom_buffer, uint32_t* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VOLUME_INTEGRATION_B200_H */

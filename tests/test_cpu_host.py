@@ -1,0 +1,74 @@
+"""CPU-only tests: the C ABI library loads and exports what its header declares,
+the drop-in Python surface matches the reference's, and the host-side checks
+raise before any device work."""
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "volume_integration_b200.h")
+LIB = os.path.join(ROOT, "volume-integration_b200", "volume_integration", "libvi_b200.so")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(vi_[a-z0-9_]+)\s*\(", text)) - {"vi_resize_fn"})
+
+
+def test_c_abi_exports_every_declared_symbol():
+    lib = ctypes.CDLL(LIB)
+    names = declared_functions()
+    assert "vi_integrate_primitives" in names and "vi_integrate_primitives_backward" in names
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_c_abi_host_checks_without_gpu():
+    lib = ctypes.CDLL(LIB)
+    lib.vi_sort_end_bit.restype = ctypes.c_int
+    # getHigherMsb of the tile counts of the benchmark images (integrator_impl.cu:47-62)
+    assert [lib.vi_sort_end_bit(t) for t in (64, 2500, 8160, 32400)] == [39, 44, 45, 47]
+    lib.vi_last_error.restype = ctypes.c_char_p
+    rc = lib.vi_get_state_layout(-1, 0, 1, 1, 1, 3, 4, None)
+    assert rc == 1 and b"layout" in lib.vi_last_error()
+
+
+def test_settings_fields_and_defaults_match_reference():
+    import volume_integration as vi
+    s = vi.IntegrationSettings()
+    expected = dict(tanfovx=1.0, tanfovy=1.0, image_height=512, image_width=512, near_plane=0.1,
+                    max_distance=100.0, primitive_scale=0.01, feature_offset=0, stencil_genus=1, grid_size=3,
+                    max_primitives_per_ray=64, occupancy_threshold=0.5, input_feature_dim=2,
+                    output_feature_dim=8, intermediate_feature_dim=32, hashgrid_levels=16,
+                    num_output_channels=3, debug=False)
+    for k, v in expected.items():
+        assert getattr(s, k) == v, k
+    assert torch.equal(s.viewmatrix, torch.eye(4)) and torch.equal(s.cam_pos, torch.zeros(3))
+    assert s.resolution.dtype == torch.int32 and s.feature_table.numel() == 0
+    names = [f for f in vi.IntegrationSettings.__dataclass_fields__]
+    assert names[:6] == ["viewmatrix", "projmatrix", "cam_pos", "tanfovx", "tanfovy", "image_height"]
+    assert hasattr(vi.VolumeIntegrator, "markVisible")
+
+
+def test_confidence_shape_checks():
+    import volume_integration as vi
+    s = vi.IntegrationSettings(grid_size=3, cam_pos=torch.zeros(3))
+    m = torch.zeros(4, 3)
+    with pytest.raises(ValueError):
+        vi.integrate_primitives(m, torch.zeros(4, 3, 9), torch.zeros(1), torch.zeros(1), torch.zeros(1), s)
+    with pytest.raises(AssertionError):
+        vi.integrate_primitives(m, torch.zeros(5, 27), torch.zeros(1), torch.zeros(1), torch.zeros(1), s)
+    with pytest.raises(AssertionError):
+        vi.integrate_primitives(m, torch.zeros(4, 2, 2, 2), torch.zeros(1), torch.zeros(1), torch.zeros(1), s)
+
+
+def test_cam_pos_must_be_cuda():
+    import volume_integration as vi
+    s = vi.IntegrationSettings(cam_pos=torch.zeros(3))
+    with pytest.raises(TypeError):
+        vi.integrate_primitives(torch.zeros(2, 3), torch.zeros(2, 27), torch.zeros(1), torch.zeros(1),
+                                torch.zeros(1), s)

@@ -1,0 +1,193 @@
+// torch binding `volume_integration._C`: the reference's three functions with
+// their exact positional signatures (reference ext.cpp:16-20,
+// integrate_primitives.h:42-139), forwarded to the C ABI of libvi_b200.so.
+// Tensors become device pointers; state buffers are uint8 tensors grown by a
+// resize callback, as the reference's resizeFunctional does
+// (integrate_primitives.cu:54-68).  Errors raise RuntimeError.
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+#include <torch/extension.h>
+
+#include <tuple>
+
+#include "volume_integration_b200.h"
+
+namespace {
+
+using torch::Tensor;
+
+char* resize_cb(void* user, size_t n) {
+  auto* t = static_cast<Tensor*>(user);
+  t->resize_({(int64_t)n});
+  return reinterpret_cast<char*>(t->data_ptr());
+}
+
+Tensor cuda_f32(const Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  return t.to(torch::kFloat32).contiguous();
+}
+Tensor cuda_i32(const Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  return t.to(torch::kInt32).contiguous();
+}
+void ok(int rc) { TORCH_CHECK(rc == VI_OK, "volume_integration: ", vi_last_error(), " (status ", rc, ")"); }
+
+std::tuple<int, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor> integrate_primitives(
+    const Tensor& means3D, const Tensor& primitive_confidences, const double primitive_scale,
+    const Tensor& viewmatrix, const Tensor& projmatrix, const Tensor& cam_pos, const double tan_fovx,
+    const double tan_fovy, const int64_t image_height, const int64_t image_width, const double near_plane,
+    const double max_distance, const Tensor& feature_table, const Tensor& resolution, const Tensor& do_hash,
+    const Tensor& primes, const int64_t feature_offset, const Tensor& linear_weights, const Tensor& linear_bias,
+    const int64_t stencil_genus, const int64_t grid_size, const int64_t max_primitives_per_ray,
+    const double occupancy_threshold, const Tensor& bg_color, const int64_t input_feature_dim,
+    const int64_t output_feature_dim, const int64_t intermediate_feature_dim, const int64_t hashgrid_levels,
+    const int64_t num_output_channels, const bool debug) {
+  TORCH_CHECK(means3D.dim() == 2 && means3D.size(1) == 3, "means3D must have shape (P, 3)");
+  const at::cuda::CUDAGuard guard(means3D.device());
+  const int P = (int)means3D.size(0), H = (int)image_height, W = (int)image_width;
+  Tensor m = cuda_f32(means3D, "means3D"), c = cuda_f32(primitive_confidences, "primitive_confidences");
+  Tensor vm = cuda_f32(viewmatrix, "viewmatrix"), pm = cuda_f32(projmatrix, "projmatrix");
+  Tensor cp = cuda_f32(cam_pos, "cam_pos"), ft = cuda_f32(feature_table, "feature_table");
+  Tensor rs = cuda_i32(resolution, "resolution"), dh = cuda_i32(do_hash, "do_hash"), pr = cuda_i32(primes, "primes");
+  Tensor lw = cuda_f32(linear_weights, "linear_weights"), lb = cuda_f32(linear_bias, "linear_bias");
+  Tensor bg = cuda_f32(bg_color, "bg_color");
+  TORCH_CHECK(vm.numel() >= 16 && pm.numel() >= 16, "viewmatrix/projmatrix need 16 elements");
+  TORCH_CHECK(rs.numel() >= hashgrid_levels && dh.numel() >= hashgrid_levels, "resolution/do_hash need L entries");
+  TORCH_CHECK(pr.numel() >= 3 && bg.numel() >= 3, "primes and bg_color need 3 entries");
+  TORCH_CHECK(c.numel() == (int64_t)P * grid_size * grid_size * grid_size, "primitive_confidences must be (P, G^3)");
+  auto fo = m.options();
+  Tensor out_color = torch::empty({(int64_t)num_output_channels, H, W}, fo);
+  Tensor out_features = torch::empty({output_feature_dim, H, W}, fo);
+  Tensor visibility = torch::empty({H, W}, fo);
+  auto bo = fo.dtype(torch::kUInt8);
+  Tensor geom = torch::empty({0}, bo), binning = torch::empty({0}, bo), img = torch::empty({0}, bo);
+  int num_rendered = 0;
+  ok(vi_integrate_primitives(
+      resize_cb, &geom, resize_cb, &binning, resize_cb, &img, out_color.data_ptr<float>(),
+      out_features.data_ptr<float>(), visibility.data_ptr<float>(), &num_rendered, P, m.data_ptr<float>(),
+      c.data_ptr<float>(), (float)primitive_scale, vm.data_ptr<float>(), pm.data_ptr<float>(), cp.data_ptr<float>(),
+      (float)tan_fovx, (float)tan_fovy, H, W, (float)near_plane, (float)max_distance, ft.data_ptr<float>(),
+      (uint64_t)ft.numel(), rs.data_ptr<int>(), dh.data_ptr<int>(), pr.data_ptr<int>(), (int)feature_offset,
+      lw.data_ptr<float>(), (uint64_t)lw.numel(), lb.data_ptr<float>(), (uint64_t)lb.numel(), (int)stencil_genus,
+      (int)grid_size, (int)max_primitives_per_ray, (float)occupancy_threshold, bg.data_ptr<float>(),
+      (unsigned)input_feature_dim, (unsigned)output_feature_dim, (unsigned)intermediate_feature_dim,
+      (unsigned)hashgrid_levels, (unsigned)num_output_channels, debug ? 1 : 0,
+      at::cuda::getCurrentCUDAStream().stream()));
+  return {num_rendered, out_color, out_features, visibility, geom, binning, img};
+}
+
+std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> integrate_primitives_backward(
+    const Tensor& dL_dout_color, const Tensor& dL_dout_features, const Tensor& geomBuffer,
+    const Tensor& binningBuffer, const Tensor& imgBuffer, const Tensor& means3D, const Tensor& primitive_confidences,
+    const double primitive_scale, const Tensor& viewmatrix, const Tensor& projmatrix, const Tensor& cam_pos,
+    const double tan_fovx, const double tan_fovy, const int64_t image_height, const int64_t image_width,
+    const double near_plane, const double max_distance, const Tensor& feature_table, const Tensor& resolution,
+    const Tensor& do_hash, const Tensor& primes, const int64_t feature_offset, const Tensor& linear_weights,
+    const Tensor& linear_bias, const int64_t stencil_genus, const int64_t grid_size,
+    const int64_t max_primitives_per_ray, const double occupancy_threshold, const Tensor& bg_color,
+    const int64_t input_feature_dim, const int64_t output_feature_dim, const int64_t hashgrid_levels,
+    const int64_t num_output_channels, const int64_t feature_table_size, const int64_t P, const int64_t num_rendered,
+    const bool debug) {
+  const at::cuda::CUDAGuard guard(means3D.device());
+  Tensor m = cuda_f32(means3D, "means3D"), c = cuda_f32(primitive_confidences, "primitive_confidences");
+  Tensor vm = cuda_f32(viewmatrix, "viewmatrix"), pm = cuda_f32(projmatrix, "projmatrix");
+  Tensor cp = cuda_f32(cam_pos, "cam_pos"), ft = cuda_f32(feature_table, "feature_table");
+  Tensor rs = cuda_i32(resolution, "resolution"), dh = cuda_i32(do_hash, "do_hash"), pr = cuda_i32(primes, "primes");
+  Tensor lw = cuda_f32(linear_weights, "linear_weights"), lb = cuda_f32(linear_bias, "linear_bias");
+  Tensor bg = cuda_f32(bg_color, "bg_color");
+  Tensor gc = cuda_f32(dL_dout_color, "dL_dout_color");
+  Tensor gf = dL_dout_features.numel() ? cuda_f32(dL_dout_features, "dL_dout_features") : dL_dout_features;
+  TORCH_CHECK(gc.numel() == 3 * image_height * image_width, "dL_dout_color must be (3, H, W)");
+  TORCH_CHECK(gf.numel() == output_feature_dim * image_height * image_width, "dL_dout_features must be (F_out, H, W)");
+  Tensor dmeans = torch::empty_like(m), dconf = torch::empty_like(c), dtable = torch::empty_like(ft);
+  Tensor dW = torch::empty_like(lw), db = torch::empty_like(lb);
+  ok(vi_integrate_primitives_backward(
+      dmeans.data_ptr<float>(), dconf.data_ptr<float>(), dtable.data_ptr<float>(), dW.data_ptr<float>(),
+      db.data_ptr<float>(), gc.data_ptr<float>(), gf.numel() ? gf.data_ptr<float>() : nullptr,
+      geomBuffer.numel() ? reinterpret_cast<char*>(geomBuffer.data_ptr()) : nullptr,
+      binningBuffer.numel() ? reinterpret_cast<char*>(binningBuffer.data_ptr()) : nullptr,
+      imgBuffer.numel() ? reinterpret_cast<char*>(imgBuffer.data_ptr()) : nullptr, m.data_ptr<float>(),
+      c.data_ptr<float>(), (float)primitive_scale, vm.data_ptr<float>(), pm.data_ptr<float>(), cp.data_ptr<float>(),
+      (float)tan_fovx, (float)tan_fovy, (int)image_height, (int)image_width, (float)near_plane, (float)max_distance,
+      ft.data_ptr<float>(), rs.data_ptr<int>(), dh.data_ptr<int>(), pr.data_ptr<int>(), (int)feature_offset,
+      lw.data_ptr<float>(), lb.data_ptr<float>(), (int)stencil_genus, (int)grid_size, (int)max_primitives_per_ray,
+      (float)occupancy_threshold, bg.data_ptr<float>(), (unsigned)input_feature_dim, (unsigned)output_feature_dim,
+      (unsigned)hashgrid_levels, (unsigned)num_output_channels, (uint64_t)feature_table_size, (int)P,
+      (int)num_rendered, debug ? 1 : 0, at::cuda::getCurrentCUDAStream().stream()));
+  return {dmeans, dconf, dtable, dW, db};
+}
+
+Tensor mark_visible(Tensor& means3D, Tensor& viewmatrix, Tensor& projmatrix) {
+  const at::cuda::CUDAGuard guard(means3D.device());
+  Tensor m = cuda_f32(means3D, "means3D"), vm = cuda_f32(viewmatrix, "viewmatrix");
+  Tensor pm = cuda_f32(projmatrix, "projmatrix");
+  Tensor present = torch::empty({m.size(0)}, m.options().dtype(torch::kBool));
+  ok(vi_mark_visible((int)m.size(0), m.data_ptr<float>(), vm.data_ptr<float>(), pm.data_ptr<float>(),
+                     reinterpret_cast<uint8_t*>(present.data_ptr()), at::cuda::getCurrentCUDAStream().stream()));
+  return present;
+}
+
+// Views of the integer state inside the forward's buffers, in the reference's
+// formats (integrator_impl.h:35-146); used by parity tests and debugging.
+py::dict state_views(const Tensor& geom, const Tensor& binning, const Tensor& img, int64_t P, int64_t R, int64_t H,
+                     int64_t W, int64_t K, int64_t G, int64_t Fout) {
+  vi_state_layout L;
+  ok(vi_get_state_layout((int)P, R, (int)H, (int)W, (int)K, (int)G, (unsigned)Fout, &L));
+  auto view = [](const Tensor& buf, size_t off, int64_t n, torch::ScalarType t) {
+    int64_t sz = n * (int64_t)c10::elementSize(t);
+    return buf.narrow(0, (int64_t)off, sz).view(t);
+  };
+  const int64_t N = H * W, tiles = ((W + 15) / 16) * ((H + 15) / 16), V = G * G * G;
+  py::dict d;
+  if (geom.numel()) {
+    d["depths"] = view(geom, L.depths, P, torch::kFloat32);
+    d["radii"] = view(geom, L.radii, P, torch::kInt32);
+    d["means2D"] = view(geom, L.means2D, 2 * P, torch::kFloat32).view({P, 2});
+    d["tiles_touched"] = view(geom, L.tiles_touched, P, torch::kInt32);
+    d["rec_cnt"] = view(geom, L.rec_cnt, P, torch::kInt32);
+    d["rec_key"] = view(geom, L.rec_key, P * V, torch::kInt32);
+    d["rec_props"] = view(geom, L.rec_props, P * V * L.props_stride, torch::kFloat32);
+    d["status"] = view(geom, L.status, 4, torch::kInt32);
+  }
+  if (binning.numel() && R > 0) {
+    d["sorted_tiles"] = view(binning, L.sorted_tiles, R, torch::kInt32);
+    d["point_list"] = view(binning, L.point_list, R, torch::kInt32);
+  }
+  if (img.numel()) {
+    d["ranges"] = view(img, L.ranges, 2 * tiles, torch::kInt32).view({tiles, 2});
+    d["final_T"] = view(img, L.final_T, N, torch::kFloat32);
+    d["n_contrib"] = view(img, L.n_contrib, N, torch::kInt32);
+    d["contrib_idx"] = view(img, L.contrib_idx, N * K, torch::kInt32);
+    d["delta_t"] = view(img, L.delta_t, N * K, torch::kFloat32);
+    d["contrib_rec"] = view(img, L.contrib_rec, N * K, torch::kInt32);
+  }
+  return d;
+}
+
+// Stable sort of int64 keys (read as uint64) with int32 values over [begin_bit, end_bit).
+std::tuple<Tensor, Tensor> sort_pairs(const Tensor& keys, const Tensor& vals, int64_t begin_bit, int64_t end_bit) {
+  TORCH_CHECK(keys.is_cuda() && keys.scalar_type() == torch::kInt64, "keys must be CUDA int64");
+  TORCH_CHECK(vals.is_cuda() && vals.scalar_type() == torch::kInt32 && vals.numel() == keys.numel(),
+              "vals must be CUDA int32 of the same length");
+  const at::cuda::CUDAGuard guard(keys.device());
+  Tensor kin = keys.contiguous().clone(), vin = vals.contiguous().clone();
+  Tensor kout = torch::empty_like(kin), vout = torch::empty_like(vin);
+  size_t tb = vi_sort_pairs_temp_bytes((uint64_t)kin.numel(), (int)begin_bit, (int)end_bit);
+  Tensor temp = torch::empty({(int64_t)tb}, kin.options().dtype(torch::kUInt8));
+  ok(vi_sort_pairs(reinterpret_cast<uint64_t*>(kin.data_ptr()), reinterpret_cast<uint32_t*>(vin.data_ptr()),
+                   reinterpret_cast<uint64_t*>(kout.data_ptr()), reinterpret_cast<uint32_t*>(vout.data_ptr()),
+                   (uint64_t)kin.numel(), (int)begin_bit, (int)end_bit, temp.data_ptr(), tb,
+                   at::cuda::getCurrentCUDAStream().stream()));
+  return {kout, vout};
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("integrate_primitives", &integrate_primitives, "Integrate Primitives CUDA forward");
+  m.def("integrate_primitives_backward", &integrate_primitives_backward, "Integrate Primitives CUDA backward");
+  m.def("mark_visible", &mark_visible, "Mark Visible Primitives CUDA");
+  m.def("state_views", &state_views, "Integer state of a forward call in the reference's formats");
+  m.def("sort_pairs", &sort_pairs, "Stable radix sort of (uint64 key, uint32 value) pairs");
+  m.def("sort_end_bit", [](int64_t tiles) { return vi_sort_end_bit((uint32_t)tiles); });
+}

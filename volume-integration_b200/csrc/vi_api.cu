@@ -1,0 +1,408 @@
+// C ABI of the renderer: argument checks, state-buffer layouts and the stage
+// order of one forward / backward call (reference
+// cuda_integrator/integrator_impl.cu:196-469 and :474-756).
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+
+#include "../../include/volume_integration_b200.h"
+#include "vi_common.cuh"
+#include "vi_internal.h"
+
+namespace vi {
+namespace {
+
+thread_local char g_err[512];
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof g_err, fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+  return fail(VI_ERR_CUDA, "%s: %s", where, cudaGetErrorString(e));
+}
+
+// Layout helper: carves consecutive 256-byte aligned arrays out of a base
+// address (or out of address 0 to measure the total size).
+struct Carver {
+  uintptr_t base, cur;
+  explicit Carver(char* b) : base((uintptr_t)b), cur(0) {}
+  template <typename T>
+  T* take(size_t count) {
+    cur = align_up(cur);
+    T* p = (T*)(base + cur);
+    cur += sizeof(T) * count;
+    return p;
+  }
+  size_t size() const { return align_up(cur) + 256; }
+};
+
+int props_stride(int O) { return O > 8 ? 16 : 8; }
+int tile_bits(size_t tiles) {
+  // getHigherMsb (integrator_impl.cu:47-62)
+  uint32_t n = (uint32_t)tiles, msb = sizeof(n) * 4, step = msb;
+  while (step > 1) {
+    step /= 2;
+    if (n >> msb) msb += step; else msb -= step;
+  }
+  if (n >> msb) msb++;
+  return (int)msb;
+}
+
+thread_local uint64_t* g_pinned = nullptr;
+thread_local cudaEvent_t g_events[64] = {};
+
+cudaEvent_t event_for_device() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!g_events[dev]) cudaEventCreateWithFlags(&g_events[dev], cudaEventDisableTiming);
+  return g_events[dev];
+}
+
+}  // namespace
+
+GeomState geom_layout(char* base, size_t P, int V, int O) {
+  GeomState g;
+  Carver c(base);
+  const int OP = props_stride(O);
+  g.status = c.take<uint32_t>(64);
+  g.depths = c.take<float>(P);
+  g.radii = c.take<int>(P);
+  g.means2D = c.take<float>(2 * P);
+  g.tiles_touched = c.take<uint32_t>(P);
+  g.dkeys = c.take<uint32_t>(P);
+  g.didx = c.take<uint32_t>(P);
+  g.dkeys_alt = c.take<uint32_t>(P);
+  g.didx_alt = c.take<uint32_t>(P);
+  g.offsets = c.take<uint32_t>(P);
+  g.block_sums = c.take<uint32_t>((P + kScanBlock - 1) / kScanBlock + 1);
+  g.rec_cnt = c.take<uint32_t>(P);
+  g.rec_key = c.take<uint32_t>(P * V);
+  g.rec_props = c.take<float>(P * V * OP);
+  g.rec_flag = c.take<uint8_t>(P * V);
+  g.rec_dpre = c.take<float>(P * V * OP);
+  char* st = c.take<char>(sort_temp_bytes(P, 4, 0, 32));
+  sort_temp_carve(st, P, 4, 0, 32, g.sort);
+  g.bytes = c.size();
+  return g;
+}
+
+BinState bin_layout(char* base, uint64_t R, int tb) {
+  BinState b;
+  Carver c(base);
+  b.tkeys = c.take<uint32_t>(R);
+  b.tvals = c.take<uint32_t>(R);
+  b.tkeys_alt = c.take<uint32_t>(R);
+  b.tvals_alt = c.take<uint32_t>(R);
+  char* st = c.take<char>(sort_temp_bytes(R, 4, 0, tb));
+  sort_temp_carve(st, R, 4, 0, tb, b.sort);
+  b.bytes = c.size();
+  return b;
+}
+
+ImgState img_layout(char* base, size_t N, int K, size_t tiles) {
+  ImgState m;
+  Carver c(base);
+  m.ranges = c.take<uint32_t>(2 * tiles);
+  m.final_T = c.take<float>(N);
+  m.n_contrib = c.take<int32_t>(N);
+  m.contrib_idx = c.take<int32_t>(N * (size_t)K);
+  m.delta_t = c.take<float>(N * (size_t)K);
+  m.contrib_rec = c.take<uint32_t>(N * (size_t)K);
+  m.bytes = c.size();
+  return m;
+}
+
+namespace {
+
+// Checks shared by forward and backward; fills the per-call constants.
+int make_scene(Scene& sc, int P, const float* means3D, const float* conf, float scale, const float* view,
+               const float* proj, float tanfovx, float tanfovy, int H, int W, float near_plane, float max_distance,
+               const float* table, const int* res, const int* do_hash, const int* primes, int T, const float* Wl,
+               const float* bl, int genus, int G, int K, const float* bg, unsigned F, unsigned Fout, unsigned L,
+               unsigned channels) {
+  if (channels != 3)
+    return fail(VI_ERR_UNSUPPORTED, "num_output_channels=%u: only 3 colour channels are implemented (as the "
+                                    "reference, forward.cu:838)", channels);
+  if (P < 0 || H < 0 || W < 0 || K < 0) return fail(VI_ERR_INVALID_ARGUMENT, "negative size (P=%d H=%d W=%d K=%d)", P, H, W, K);
+  if (G < 1 || G > 3)
+    return fail(VI_ERR_UNSUPPORTED, "grid_size=%d: the kernels map one grid point per lane and need 1 <= G <= 3", G);
+  if (!(F == 1 || F == 2 || F == 4 || F == 8))
+    return fail(VI_ERR_UNSUPPORTED, "input_feature_dim=%u: supported values are 1, 2, 4, 8", F);
+  if (L < 1 || L * F > 64) return fail(VI_ERR_UNSUPPORTED, "hashgrid_levels*input_feature_dim=%u must be in [1, 64]", L * F);
+  if (Fout > 12) return fail(VI_ERR_UNSUPPORTED, "output_feature_dim=%u: at most 12 is supported", Fout);
+  if (T <= 0) return fail(VI_ERR_INVALID_ARGUMENT, "feature_offset=%d must be positive", T);
+  if ((size_t)W * H >= (1ull << 31)) return fail(VI_ERR_UNSUPPORTED, "image of %d x %d pixels is too large", W, H);
+  if (P > 0 && (!means3D || !conf || !view || !proj || !table || !res || !do_hash || !primes || !Wl || !bl || !bg))
+    return fail(VI_ERR_INVALID_ARGUMENT, "a required input pointer is NULL");
+  sc.P = P; sc.W = W; sc.H = H; sc.G = G; sc.V = G * G * G;
+  sc.L = (int)L; sc.F = (int)F; sc.D = (int)(L * F); sc.Fout = (int)Fout; sc.O = (int)Fout + 4;
+  sc.K = K; sc.genus = genus;
+  sc.T = (uint32_t)T;
+  sc.Tmask = ((uint32_t)T & ((uint32_t)T - 1)) == 0 ? (uint32_t)T - 1 : 0u;
+  sc.scale = scale;
+  sc.step = G > 1 ? scale / (float)(G - 1) : scale;  // forward.cu:395
+  sc.gof = (float)(G - 1) / 2.0f;                    // forward.cu:396
+  sc.near_plane = near_plane; sc.max_distance = max_distance;
+  sc.focal_y = (float)H / (2.0f * tanfovy);  // integrator_impl.cu:273-274
+  sc.focal_x = (float)W / (2.0f * tanfovx);
+  sc.means = means3D; sc.conf = conf; sc.view = view; sc.proj = proj; sc.table = table;
+  sc.res = res; sc.do_hash = do_hash; sc.primes = primes; sc.Wl = Wl; sc.bl = bl; sc.bg = bg;
+  sc.gx = (unsigned)(W + VI_TILE - 1) / VI_TILE;
+  sc.gy = (unsigned)(H + VI_TILE - 1) / VI_TILE;
+  return VI_OK;
+}
+
+int check(cudaStream_t s, int debug, const char* where, const uint32_t* status) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, where);
+  if (debug) {
+    e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(e, where);
+    if (status) {
+      uint32_t st = 0;
+      cudaMemcpy(&st, status, 4, cudaMemcpyDeviceToHost);
+      if (st) return fail(VI_ERR_DEVICE, "%s: device status 0x%x", where, st);
+    }
+  }
+  return VI_OK;
+}
+
+}  // namespace
+}  // namespace vi
+
+using namespace vi;
+
+extern "C" const char* vi_last_error(void) { return g_err; }
+
+extern "C" int vi_sort_end_bit(uint32_t num_tiles) { return 32 + tile_bits(num_tiles); }
+
+extern "C" int vi_integrate_primitives(
+    vi_resize_fn geom_buffer, void* geom_user, vi_resize_fn binning_buffer, void* binning_user,
+    vi_resize_fn img_buffer, void* img_user, float* out_color, float* out_features, float* visibility_info,
+    int* num_rendered, int P, const float* means3D, const float* primitive_confidences, float primitive_scale,
+    const float* viewmatrix, const float* projmatrix, const float* cam_pos, float tan_fovx, float tan_fovy,
+    int image_height, int image_width, float near_plane, float max_distance, const float* feature_table,
+    uint64_t feature_table_numel, const int* resolution, const int* do_hash, const int* primes, int feature_offset,
+    const float* linear_weights, uint64_t linear_weights_numel, const float* linear_bias,
+    uint64_t linear_bias_numel, int stencil_genus, int grid_size, int max_primitives_per_ray,
+    float occupancy_threshold, const float* bg_color, unsigned input_feature_dim, unsigned output_feature_dim,
+    unsigned intermediate_feature_dim, unsigned hashgrid_levels, unsigned num_output_channels, int debug,
+    void* stream) {
+  (void)cam_pos;
+  (void)occupancy_threshold;  // has no effect in the reference either (forward.cu:118-140 is never called)
+  cudaStream_t s = (cudaStream_t)stream;
+  if (!num_rendered || !geom_buffer || !binning_buffer || !img_buffer)
+    return fail(VI_ERR_INVALID_ARGUMENT, "num_rendered and the three buffer callbacks are required");
+  *num_rendered = 0;
+  Scene sc;
+  int rc = make_scene(sc, P, means3D, primitive_confidences, primitive_scale, viewmatrix, projmatrix, tan_fovx,
+                      tan_fovy, image_height, image_width, near_plane, max_distance, feature_table, resolution,
+                      do_hash, primes, feature_offset, linear_weights, linear_bias, stencil_genus, grid_size,
+                      max_primitives_per_ray, bg_color, input_feature_dim, output_feature_dim, hashgrid_levels,
+                      num_output_channels);
+  if (rc) return rc;
+  if (intermediate_feature_dim != hashgrid_levels * input_feature_dim)
+    return fail(VI_ERR_INVALID_ARGUMENT,
+                "intermediate_feature_dim=%u must equal hashgrid_levels*input_feature_dim=%u (the reference reads "
+                "uninitialised weights otherwise, forward.cu:326-331 vs :457)",
+                intermediate_feature_dim, hashgrid_levels * input_feature_dim);
+  if (feature_table_numel < (uint64_t)sc.T * sc.L * sc.F)
+    return fail(VI_ERR_INVALID_ARGUMENT, "feature_table has %llu elements, needs feature_offset*L*F=%llu",
+                (unsigned long long)feature_table_numel, (unsigned long long)sc.T * sc.L * sc.F);
+  if (linear_weights_numel < (uint64_t)sc.O * sc.D || linear_bias_numel < (uint64_t)sc.O)
+    return fail(VI_ERR_INVALID_ARGUMENT, "linear layer needs %d weights and %d biases, got %llu and %llu",
+                sc.O * sc.D, sc.O, (unsigned long long)linear_weights_numel, (unsigned long long)linear_bias_numel);
+  const size_t N = (size_t)sc.W * sc.H;
+  if (P == 0 || N == 0) {
+    // integrate_primitives.cu:153-190: zero images, empty state.
+    if (N) {
+      cudaMemsetAsync(out_color, 0, 3 * N * sizeof(float), s);
+      if (sc.Fout) cudaMemsetAsync(out_features, 0, sc.Fout * N * sizeof(float), s);
+      cudaMemsetAsync(visibility_info, 0, N * sizeof(float), s);
+    }
+    return check(s, debug, "empty forward", nullptr);
+  }
+  const size_t tiles = (size_t)sc.gx * sc.gy;
+
+  GeomState g = geom_layout(nullptr, P, sc.V, sc.O);
+  char* gb = geom_buffer(geom_user, g.bytes);
+  if (!gb) return fail(VI_ERR_ALLOC, "geometry buffer of %zu bytes", g.bytes);
+  g = geom_layout(gb, P, sc.V, sc.O);
+  ImgState im = img_layout(nullptr, N, sc.K, tiles);
+  char* ib = img_buffer(img_user, im.bytes);
+  if (!ib) return fail(VI_ERR_ALLOC, "image buffer of %zu bytes", im.bytes);
+  im = img_layout(ib, N, sc.K, tiles);
+
+  cudaMemsetAsync(g.status, 0, 64 * sizeof(uint32_t), s);
+  launch_preprocess(sc, g, s);
+  if ((rc = check(s, debug, "preprocess", g.status))) return rc;
+  const bool depth_alt =
+      onesweep_sort_u32(g.dkeys, g.didx, g.dkeys_alt, g.didx_alt, (uint64_t)P, 0, 32, g.sort, g.status, s);
+  const uint32_t* sorted_idx = depth_alt ? g.didx_alt : g.didx;
+  if ((rc = check(s, debug, "depth sort", g.status))) return rc;
+  launch_offsets_scan(sc, g, sorted_idx, s);
+  if (!g_pinned) {
+    cudaError_t e = cudaHostAlloc((void**)&g_pinned, 64, cudaHostAllocPortable);
+    if (e != cudaSuccess) return cuda_fail(e, "pinned staging buffer");
+  }
+  cudaMemcpyAsync(g_pinned, g.status, 16, cudaMemcpyDeviceToHost, s);
+  cudaEvent_t ev = event_for_device();
+  cudaEventRecord(ev, s);
+  // The feature stage depends only on preprocess: queue it before blocking on
+  // the overlap count so the GPU works while the host waits.
+  launch_features(sc, g, s);
+  if ((rc = check(s, debug, "features", g.status))) return rc;
+  cudaError_t e = cudaEventSynchronize(ev);
+  if (e != cudaSuccess) return cuda_fail(e, "overlap count readback");
+  const uint32_t st0 = (uint32_t)(g_pinned[0] & 0xffffffffu);
+  const uint64_t R = g_pinned[1];
+  if (st0) return fail(VI_ERR_DEVICE, "device status 0x%x after binning", st0);
+  if (R >= (1ull << 30)) return fail(VI_ERR_TOO_MANY_OVERLAPS, "%llu overlaps exceed 2^30", (unsigned long long)R);
+
+  const int tb = tile_bits(tiles);
+  BinState b = bin_layout(nullptr, R, tb);
+  char* bb = binning_buffer(binning_user, b.bytes);
+  if (!bb) return fail(VI_ERR_ALLOC, "binning buffer of %zu bytes", b.bytes);
+  b = bin_layout(bb, R, tb);
+  const uint32_t* point_list = b.tvals;
+  const uint32_t* sorted_tiles = b.tkeys;
+  if (R > 0) {
+    launch_duplicate(sc, g, sorted_idx, b, s);
+    if ((rc = check(s, debug, "duplicate", g.status))) return rc;
+    const bool alt = onesweep_sort_u32(b.tkeys, b.tvals, b.tkeys_alt, b.tvals_alt, R, 0, tb, b.sort, g.status, s);
+    point_list = alt ? b.tvals_alt : b.tvals;
+    sorted_tiles = alt ? b.tkeys_alt : b.tkeys;
+    if ((rc = check(s, debug, "tile sort", g.status))) return rc;
+  }
+  launch_ranges(R, sorted_tiles, im.ranges, tiles, s);
+  launch_render(sc, g, point_list, im, out_color, out_features, visibility_info, s);
+  if ((rc = check(s, debug, "render", g.status))) return rc;
+  *num_rendered = (int)R;
+  return VI_OK;
+}
+
+extern "C" int vi_integrate_primitives_backward(
+    float* dL_dmeans3D, float* dL_dconfidences, float* dL_dfeature_table, float* dL_dlinear_weights,
+    float* dL_dlinear_bias, const float* dL_dout_color, const float* dL_dout_features, char* geom_buffer,
+    char* binning_buffer, char* img_buffer, const float* means3D, const float* primitive_confidences,
+    float primitive_scale, const float* viewmatrix, const float* projmatrix, const float* cam_pos, float tan_fovx,
+    float tan_fovy, int image_height, int image_width, float near_plane, float max_distance,
+    const float* feature_table, const int* resolution, const int* do_hash, const int* primes, int feature_offset,
+    const float* linear_weights, const float* linear_bias, int stencil_genus, int grid_size,
+    int max_primitives_per_ray, float occupancy_threshold, const float* bg_color, unsigned input_feature_dim,
+    unsigned output_feature_dim, unsigned hashgrid_levels, unsigned num_output_channels,
+    uint64_t feature_table_size, int P, int num_rendered, int debug, void* stream) {
+  (void)cam_pos;
+  (void)occupancy_threshold;
+  (void)binning_buffer;  // the backward walks per-pixel contributor lists, not tile lists
+  cudaStream_t s = (cudaStream_t)stream;
+  Scene sc;
+  int rc = make_scene(sc, P, means3D, primitive_confidences, primitive_scale, viewmatrix, projmatrix, tan_fovx,
+                      tan_fovy, image_height, image_width, near_plane, max_distance, feature_table, resolution,
+                      do_hash, primes, feature_offset, linear_weights, linear_bias, stencil_genus, grid_size,
+                      max_primitives_per_ray, bg_color, input_feature_dim, output_feature_dim, hashgrid_levels,
+                      num_output_channels);
+  if (rc) return rc;
+  if (feature_table_size < (uint64_t)sc.T * sc.L * sc.F)
+    return fail(VI_ERR_INVALID_ARGUMENT, "feature_table_size=%llu < feature_offset*L*F", (unsigned long long)feature_table_size);
+  // Zeroed outputs (integrator_impl.cu:573-577).
+  if (P > 0) {
+    cudaMemsetAsync(dL_dmeans3D, 0, (size_t)P * 3 * sizeof(float), s);
+    cudaMemsetAsync(dL_dconfidences, 0, (size_t)P * sc.V * sizeof(float), s);
+  }
+  cudaMemsetAsync(dL_dfeature_table, 0, feature_table_size * sizeof(float), s);
+  cudaMemsetAsync(dL_dlinear_weights, 0, (size_t)sc.O * sc.D * sizeof(float), s);
+  cudaMemsetAsync(dL_dlinear_bias, 0, (size_t)sc.O * sizeof(float), s);
+  const size_t N = (size_t)sc.W * sc.H;
+  if (num_rendered <= 0 || P == 0 || N == 0) return check(s, debug, "empty backward", nullptr);
+  if (!geom_buffer || !img_buffer) return fail(VI_ERR_INVALID_ARGUMENT, "forward state buffers are required");
+  GeomState g = geom_layout(geom_buffer, P, sc.V, sc.O);
+  ImgState im = img_layout(img_buffer, N, sc.K, (size_t)sc.gx * sc.gy);
+  launch_backward(sc, g, im, dL_dout_color, sc.Fout ? dL_dout_features : nullptr, dL_dconfidences,
+                  dL_dfeature_table, dL_dlinear_weights, dL_dlinear_bias, s);
+  return check(s, debug, "backward", g.status);
+}
+
+extern "C" int vi_mark_visible(int P, const float* means3D, const float* viewmatrix, const float* projmatrix,
+                               uint8_t* present, void* stream) {
+  (void)projmatrix;
+  if (P < 0) return fail(VI_ERR_INVALID_ARGUMENT, "P=%d", P);
+  launch_mark_visible(P, means3D, viewmatrix, (bool*)present, (cudaStream_t)stream);
+  return check((cudaStream_t)stream, 0, "mark_visible", nullptr);
+}
+
+extern "C" size_t vi_sort_pairs_temp_bytes(uint64_t n, int begin_bit, int end_bit) {
+  return sort_temp_bytes(n, 8, begin_bit, end_bit) + 512;
+}
+
+extern "C" int vi_sort_pairs(uint64_t* keys_in, uint32_t* vals_in, uint64_t* keys_out, uint32_t* vals_out, uint64_t n,
+                             int begin_bit, int end_bit, void* temp, size_t temp_bytes, void* stream) {
+  cudaStream_t s = (cudaStream_t)stream;
+  if (n >= (1ull << 30)) return fail(VI_ERR_INVALID_ARGUMENT, "n=%llu must be < 2^30", (unsigned long long)n);
+  if (begin_bit < 0 || end_bit > 64 || begin_bit > end_bit) return fail(VI_ERR_INVALID_ARGUMENT, "bit range [%d,%d)", begin_bit, end_bit);
+  if (temp_bytes < vi_sort_pairs_temp_bytes(n, begin_bit, end_bit)) return fail(VI_ERR_INVALID_ARGUMENT, "temp too small");
+  if (n == 0) return VI_OK;
+  char* t = (char*)(((uintptr_t)temp + 255) / 256 * 256);
+  uint32_t* status = (uint32_t*)t;  // first 256 bytes
+  SortTemp st;
+  sort_temp_carve(t + 256, n, 8, begin_bit, end_bit, st);
+  cudaMemsetAsync(status, 0, 4, s);
+  bool alt = onesweep_sort_u64(keys_in, vals_in, keys_out, vals_out, n, begin_bit, end_bit, st, status, s);
+  if (!alt) {
+    cudaMemcpyAsync(keys_out, keys_in, n * 8, cudaMemcpyDeviceToDevice, s);
+    cudaMemcpyAsync(vals_out, vals_in, n * 4, cudaMemcpyDeviceToDevice, s);
+  }
+  return check(s, 0, "sort_pairs", nullptr);
+}
+
+extern "C" int vi_get_state_layout(int P, int64_t num_rendered, int image_height, int image_width,
+                                   int max_primitives_per_ray, int grid_size, unsigned output_feature_dim,
+                                   vi_state_layout* out) {
+  if (!out || P < 0 || num_rendered < 0 || grid_size < 1) return fail(VI_ERR_INVALID_ARGUMENT, "bad layout query");
+  const int V = grid_size * grid_size * grid_size, O = (int)output_feature_dim + 4;
+  const size_t N = (size_t)image_width * image_height;
+  const size_t tiles = (size_t)((image_width + 15) / 16) * ((image_height + 15) / 16);
+  GeomState g = geom_layout(nullptr, P, V, O);
+  const int tb = tile_bits(tiles);
+  BinState b = bin_layout(nullptr, (uint64_t)num_rendered, tb);
+  ImgState m = img_layout(nullptr, N, max_primitives_per_ray, tiles);
+  out->geom_bytes = g.bytes;
+  out->binning_bytes = b.bytes;
+  out->img_bytes = m.bytes;
+  out->status = (size_t)g.status;
+  out->depths = (size_t)g.depths;
+  out->radii = (size_t)g.radii;
+  out->means2D = (size_t)g.means2D;
+  out->tiles_touched = (size_t)g.tiles_touched;
+  out->rec_cnt = (size_t)g.rec_cnt;
+  out->rec_key = (size_t)g.rec_key;
+  out->rec_props = (size_t)g.rec_props;
+  out->props_stride = props_stride(O);
+  // The tile sort runs ceil(bits/8) passes; an odd count leaves the result in the alternate arrays.
+  const bool alt = num_rendered > 1 && (((tb + 7) / 8) & 1);
+  out->sorted_tiles = (size_t)(alt ? b.tkeys_alt : b.tkeys);
+  out->point_list = (size_t)(alt ? b.tvals_alt : b.tvals);
+  out->ranges = (size_t)m.ranges;
+  out->final_T = (size_t)m.final_T;
+  out->n_contrib = (size_t)m.n_contrib;
+  out->contrib_idx = (size_t)m.contrib_idx;
+  out->delta_t = (size_t)m.delta_t;
+  out->contrib_rec = (size_t)m.contrib_rec;
+  return VI_OK;
+}
+
+extern "C" int vi_read_device_status(const char* geom_buffer, uint32_t* status, void* stream) {
+  GeomState g = geom_layout((char*)geom_buffer, 0, 1, 4);
+  cudaError_t e = cudaMemcpyAsync(status, g.status, 4, cudaMemcpyDeviceToHost, (cudaStream_t)stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
+  return e == cudaSuccess ? VI_OK : cuda_fail(e, "read status");
+}

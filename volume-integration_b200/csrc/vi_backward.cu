@@ -1,0 +1,457 @@
+// Backward pass (reference cuda_integrator/backward.cu:51-792, hashgrid.h:9-96).
+//
+// The reference walks every tile entry in reverse, recomputes stage 1 for it and
+// lets the pixels that list it as their next contributor accumulate gradients
+// with global atomics.  The same quantities are computed here in two kernels:
+//
+//  1. backward_pixel: one thread per pixel walks its own contributors in
+//     reverse (the pixel's state dL/dout and accum_after evolve exactly as in
+//     backward.cu:771-778) and writes dL/d(pre-activation) of each contributing
+//     (primitive, pixel) record.  Blend and density come from the forward record
+//     (identical to the reference's recompute when the forward and backward
+//     projections put every grid point in the same pixel; otherwise the
+//     record is recomputed with the backward projection).
+//  2. backward_prim: one warp per primitive, lane = grid point, gathers its
+//     contributing records and produces
+//       dconf[q,g]  = sum_p (dIn_p . phi_g) * g'_{p,g}                (backward.cu:697-710)
+//       dtable      += (sum_p dIn_p * g'_{p,g} * conf_g) * corner weight (hashgrid.h:43-95)
+//       dW, db      += dpre_p (x) in_p, dpre_p                          (backward.cu:621-641)
+//     where g' is the stencil magnitude of "neighbour's screen point lies in
+//     pixel p" (backward.cu:644-689).  The table scatter is linear in dIn, so
+//     each grid point scatters once per level and corner instead of once per
+//     pixel, and lanes hitting the same entry are reduced inside the warp before
+//     one vector atomic.  dW/db are reduced per CTA before global atomics.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "vi_kernels.cuh"
+
+namespace vi {
+namespace {
+
+// Generic (runtime F) hashgrid features, used only on the rare recompute path.
+__device__ void gather_generic(const Scene& sc, float3 pos, float* phi) {
+  const uint32_t p0 = (uint32_t)sc.primes[0], p1 = (uint32_t)sc.primes[1], p2 = (uint32_t)sc.primes[2];
+  for (int l = 0; l < sc.L; l++) {
+    const int res = sc.res[l];
+    const bool hsh = sc.do_hash[l] != 0;
+    int3 b;
+    float3 t;
+    level_setup(pos, res, b, t);
+    for (int f = 0; f < sc.F; f++) phi[l * sc.F + f] = 0.0f;
+    for (int dx = 0; dx < 2; dx++) {
+      float wx = dx == 0 ? 1.0f - t.x : t.x;
+      for (int dy = 0; dy < 2; dy++) {
+        float wy = dy == 0 ? 1.0f - t.y : t.y;
+        for (int dz = 0; dz < 2; dz++) {
+          float wz = dz == 0 ? 1.0f - t.z : t.z;
+          float w = wx * wy * wz;
+          int e = corner_entry(b.x + dx, b.y + dy, b.z + dz, res, hsh, p0, p1, p2, sc.T, sc.Tmask);
+          if (e >= 0) {
+            const float* src = sc.table + ((size_t)e * sc.L + l) * sc.F;
+            for (int f = 0; f < sc.F; f++) phi[l * sc.F + f] += src[f] * w;
+          }
+        }
+      }
+    }
+  }
+}
+
+// Activated properties of primitive q seen from pixel (px, py) with the backward
+// projection 1/w (backward.cu:404-569).
+template <int OMAX>
+__device__ void recompute_props(const Scene& sc, uint32_t q, int px, int py, float* props) {
+  const int V = sc.V, G = sc.G, D = sc.D, O = sc.O;
+  const Stencil st = make_stencil(sc.genus);
+  float conf[32];
+  uint32_t posm = 0;
+  for (int g = 0; g < V; g++) {
+    conf[g] = sc.conf[(size_t)q * V + g];
+    if (conf[g] > 0.0f) posm |= 1u << g;
+  }
+  const float3 c = make_float3(sc.means[3 * q], sc.means[3 * q + 1], sc.means[3 * q + 2]);
+  float acc[OMAX];
+  for (int o = 0; o < OMAX; o++) acc[o] = 0.0f;
+  float phi[64];
+  for (int g = 0; g < V; g++) {
+    if (!(conf[g] > 0.0f)) continue;
+    const float3 pos = grid_pos(c, g, G, sc.step, sc.gof);
+    const float2 sb = project(pos, sc.proj, sc.W, sc.H, false);
+    if (pix_coord(sb.x) != px || pix_coord(sb.y) != py) continue;
+    const float mag = occ_mag(posm, g, G, st);
+    if (!(mag > 1e-7f)) continue;
+    gather_generic(sc, pos, phi);
+    const float wgt = fmul(conf[g], mag);
+    for (int o = 0; o < O; o++) {
+      float s = 0.0f;
+      for (int i = 0; i < D; i++) s += sc.Wl[o * D + i] * phi[i];
+      acc[o] = fadd(acc[o], fmul(s, wgt));
+    }
+  }
+  for (int o = 0; o < OMAX; o++) {
+    const float pre = fadd(acc[o], sc.bl[o < O ? o : 0]);
+    props[o] = o < O - 1 ? sigmoidf_(pre) : (o == O - 1 ? expf(pre) : 0.0f);
+  }
+}
+
+template <int OMAX>
+__global__ void __launch_bounds__(256) backward_pixel_kernel(Scene sc, GeomState g, ImgState im,
+                                                            const float* __restrict__ dL_dcolor,
+                                                            const float* __restrict__ dL_dfeat) {
+  const size_t N = (size_t)sc.W * sc.H;
+  const size_t pix = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (pix >= N) return;
+  const int K = sc.K;
+  int nc = min(im.n_contrib[pix], K);
+  if (nc <= 0) return;
+  const int O = sc.O, B = O - 1, Fout = sc.Fout, V = sc.V;
+  float dOut[OMAX - 1], after[OMAX - 1];
+#pragma unroll
+  for (int d = 0; d < OMAX - 1; d++) {
+    dOut[d] = 0.0f;
+    after[d] = 0.0f;
+  }
+  dOut[0] = dL_dcolor[pix];
+  dOut[1] = dL_dcolor[N + pix];
+  dOut[2] = dL_dcolor[2 * N + pix];
+  after[0] = sc.bg[0];
+  after[1] = sc.bg[1];
+  after[2] = sc.bg[2];
+#pragma unroll
+  for (int f = 0; f < OMAX - 4; f++)
+    if (f < Fout) dOut[3 + f] = dL_dfeat ? dL_dfeat[f * N + pix] : 0.0f;
+  const int px = (int)(pix % sc.W), py = (int)(pix / sc.W);
+  for (int k = nc - 1; k >= 0; k--) {
+    const uint32_t rec = im.contrib_rec[pix * K + k];
+    const float dt = im.delta_t[pix * K + k];
+    const uint32_t q = rec / V;
+    float props[OMAX];
+    if (g.rec_cnt[q] & kBwdDiffers) {
+      recompute_props<OMAX>(sc, q, px, py, props);
+    } else {
+      const float4* src = reinterpret_cast<const float4*>(g.rec_props + (size_t)rec * OMAX);
+#pragma unroll
+      for (int o4 = 0; o4 < OMAX / 4; o4++) {
+        float4 v = src[o4];
+        props[4 * o4] = v.x; props[4 * o4 + 1] = v.y; props[4 * o4 + 2] = v.z; props[4 * o4 + 3] = v.w;
+      }
+    }
+    float dens = 0.0f;
+#pragma unroll
+    for (int o = 0; o < OMAX; o++)
+      if (o == B) dens = props[o];
+    float dalpha = 0.0f, dpre[OMAX];
+#pragma unroll
+    for (int d = 0; d < OMAX - 1; d++) {
+      if (d < B) {
+        const float y = props[d];
+        const float dbl = dOut[d] * y;
+        dalpha += dbl * (y - after[d]);
+        dpre[d] = dbl * y * (1.0f - y);
+      }
+    }
+#pragma unroll
+    for (int o = 0; o < OMAX; o++) {
+      if (o == B) dpre[o] = dalpha * dens * dt * dens;
+      else if (o > B) dpre[o] = 0.0f;
+    }
+    float4* dst = reinterpret_cast<float4*>(g.rec_dpre + (size_t)rec * OMAX);
+#pragma unroll
+    for (int o4 = 0; o4 < OMAX / 4; o4++) dst[o4] = make_float4(dpre[4 * o4], dpre[4 * o4 + 1], dpre[4 * o4 + 2], dpre[4 * o4 + 3]);
+    g.rec_flag[rec] = 1;
+#pragma unroll
+    for (int d = 0; d < OMAX - 1; d++) {
+      if (d < B) {
+        const float y = props[d];
+        dOut[d] *= y;
+        after[d] = y + after[d] * (1.0f - y);
+      }
+    }
+  }
+}
+
+// Sums F values over the lanes of each distinct table address, then one vector
+// atomic per address.  Falls back to plain per-lane atomics when addresses are
+// mostly distinct.
+template <int F>
+__device__ __forceinline__ void scatter_add(float* __restrict__ dst_base, int e, bool act, const float* v, size_t stride,
+                                            uint32_t lane) {
+  const uint32_t am = __ballot_sync(0xffffffffu, act);
+  if (!am) return;
+  const uint32_t key = act ? (uint32_t)e : 0xffffffffu - lane;
+  const uint32_t peers = __match_any_sync(0xffffffffu, key);
+  const bool lead = act && (peers & ((1u << lane) - 1)) == 0;
+  const int nlead = __popc(__ballot_sync(0xffffffffu, lead));
+  auto atomic_vec = [&](float* p, const float* x) {
+    if constexpr (F == 2) {
+      atomicAdd(reinterpret_cast<float2*>(p), make_float2(x[0], x[1]));
+    } else if constexpr (F == 4) {
+      atomicAdd(reinterpret_cast<float4*>(p), make_float4(x[0], x[1], x[2], x[3]));
+    } else if constexpr (F == 8) {
+      atomicAdd(reinterpret_cast<float4*>(p), make_float4(x[0], x[1], x[2], x[3]));
+      atomicAdd(reinterpret_cast<float4*>(p) + 1, make_float4(x[4], x[5], x[6], x[7]));
+    } else {
+#pragma unroll
+      for (int f = 0; f < F; f++) atomicAdd(p + f, x[f]);
+    }
+  };
+  if (nlead * 4 <= __popc(am)) {
+    uint32_t rem = am;
+    while (rem) {
+      const int l0 = __ffs(rem) - 1;
+      const uint32_t k0 = __shfl_sync(0xffffffffu, key, l0);
+      const bool in = act && key == k0;
+      float x[F];
+#pragma unroll
+      for (int f = 0; f < F; f++) {
+        float y = in ? v[f] : 0.0f;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) y += __shfl_xor_sync(0xffffffffu, y, off);
+        x[f] = y;
+      }
+      if ((int)lane == l0) atomic_vec(dst_base + (size_t)k0 * stride, x);
+      rem &= ~__ballot_sync(0xffffffffu, in);
+    }
+  } else if (act) {
+    atomic_vec(dst_base + (size_t)e * stride, v);
+  }
+}
+
+constexpr int kBwdWarps = 4;
+
+template <int F, int OMAX>
+__global__ void __launch_bounds__(kBwdWarps * 32) backward_prim_kernel(Scene sc, GeomState g, float* __restrict__ dconf,
+                                                                      float* __restrict__ dtable, float* __restrict__ dW,
+                                                                      float* __restrict__ db) {
+  extern __shared__ float smem[];
+  const int L = sc.L, D = L * F, O = sc.O, V = sc.V, G = sc.G;
+  const int DS = D + 1;
+  float* W_s = smem;                 // [O][D]
+  float* dW_s = W_s + OMAX * D;      // [OMAX][D]
+  float* db_s = dW_s + OMAX * D;     // [OMAX]
+  const int w = threadIdx.x >> 5;
+  const uint32_t lane = threadIdx.x & 31;
+  float* phi_s = db_s + OMAX + w * (2 * 32 * DS + 32 * OMAX + 64);
+  float* A_s = phi_s + 32 * DS;
+  float* E_s = A_s + 32 * DS;
+  float* dIn_s = E_s + 32 * OMAX;  // [64]
+
+  for (int i = threadIdx.x; i < OMAX * D; i += blockDim.x) {
+    W_s[i] = i < O * D ? sc.Wl[i] : 0.0f;
+    dW_s[i] = 0.0f;
+  }
+  for (int i = threadIdx.x; i < OMAX; i += blockDim.x) db_s[i] = 0.0f;
+  __syncthreads();
+
+  const Stencil st = make_stencil(sc.genus);
+  const uint32_t p0 = (uint32_t)sc.primes[0], p1 = (uint32_t)sc.primes[1], p2 = (uint32_t)sc.primes[2];
+  float dWacc[2][OMAX];
+#pragma unroll
+  for (int h = 0; h < 2; h++)
+#pragma unroll
+    for (int o = 0; o < OMAX; o++) dWacc[h][o] = 0.0f;
+  float dbacc = 0.0f;
+
+  const int nwarps = gridDim.x * kBwdWarps;
+  for (int q = blockIdx.x * kBwdWarps + w; q < sc.P; q += nwarps) {
+    const uint32_t n = g.rec_cnt[q] & ~kBwdDiffers;
+    if (n == 0) continue;
+    const size_t s0 = (size_t)q * V;
+    const uint32_t cm = __ballot_sync(0xffffffffu, lane < n && g.rec_flag[s0 + lane] != 0);
+    if (cm == 0) continue;
+
+    const bool act = (int)lane < V;
+    const float conf = act ? sc.conf[s0 + lane] : 0.0f;
+    const float3 c = make_float3(sc.means[3 * q], sc.means[3 * q + 1], sc.means[3 * q + 2]);
+    const float3 pos = grid_pos(c, act ? (int)lane : 0, G, sc.step, sc.gof);
+    const float2 sb = project(pos, sc.proj, sc.W, sc.H, false);
+    const int bx = pix_coord(sb.x), by = pix_coord(sb.y);
+    const int bpix = (act && bx >= 0 && bx < sc.W && by >= 0 && by < sc.H) ? by * sc.W + bx : -1;
+    const uint32_t posm = __ballot_sync(0xffffffffu, act && conf > 0.0f);
+    const float mag = act ? occ_mag(posm, lane, G, st) : 0.0f;
+    const float wE = (act && conf > 0.0f && mag > 1e-7f) ? fmul(conf, mag) : 0.0f;
+
+    // Which lanes matter: own pixel contributing, or a stencil neighbour in one.
+    bool involved = false;
+    {
+      uint32_t m = cm;
+      while (m) {
+        const int j = __ffs(m) - 1;
+        m &= m - 1;
+        const uint32_t key = g.rec_key[s0 + j];
+        const uint32_t t = key >> 8;
+        const int ppx = (int)((t % sc.gx) * 16 + (key & 15u)), ppy = (int)((t / sc.gx) * 16 + ((key >> 4) & 15u));
+        const uint32_t inm = __ballot_sync(0xffffffffu, bpix == ppy * sc.W + ppx);
+        if (act && occ_mag(inm, lane, G, st) > 0.0f) involved = true;
+        if ((inm >> lane) & 1u) involved = true;
+      }
+    }
+    float* phi = phi_s + lane * DS;
+    float* A = A_s + lane * DS;
+    if (involved) {
+      gather_features<F>(sc, pos, phi);
+      for (int i = 0; i < D; i++) A[i] = 0.0f;
+    }
+#pragma unroll
+    for (int o = 0; o < OMAX; o++) E_s[lane * OMAX + o] = 0.0f;
+    float dX = 0.0f;
+    bool hasA = false;
+    __syncwarp();
+
+    uint32_t m = cm;
+    while (m) {
+      const int j = __ffs(m) - 1;
+      m &= m - 1;
+      const size_t slot = s0 + j;
+      const uint32_t key = g.rec_key[slot];
+      const uint32_t t = key >> 8;
+      const int ppx = (int)((t % sc.gx) * 16 + (key & 15u)), ppy = (int)((t / sc.gx) * 16 + ((key >> 4) & 15u));
+      float dpre[OMAX];
+      const float4* src = reinterpret_cast<const float4*>(g.rec_dpre + slot * OMAX);
+#pragma unroll
+      for (int o4 = 0; o4 < OMAX / 4; o4++) {
+        float4 v = src[o4];
+        dpre[4 * o4] = v.x; dpre[4 * o4 + 1] = v.y; dpre[4 * o4 + 2] = v.z; dpre[4 * o4 + 3] = v.w;
+      }
+#pragma unroll
+      for (int o = 0; o < OMAX; o++)
+        if ((int)lane == o) dbacc += dpre[o];
+      const uint32_t inm = __ballot_sync(0xffffffffu, bpix == ppy * sc.W + ppx);
+      if (((inm >> lane) & 1u) && wE != 0.0f) {
+#pragma unroll
+        for (int o = 0; o < OMAX; o++) E_s[lane * OMAX + o] = fmul(wE, dpre[o]);
+      }
+      for (int jj = lane; jj < D; jj += 32) {
+        float s = 0.0f;
+#pragma unroll
+        for (int o = 0; o < OMAX; o++) s += dpre[o] * W_s[o * D + jj];
+        dIn_s[jj] = s;
+      }
+      __syncwarp();
+      const float gp = act ? occ_mag(inm, lane, G, st) : 0.0f;
+      if (gp > 1e-7f) {
+        const float wp = fmul(gp, conf);
+        const bool doA = fabsf(wp) > 1e-9f;
+        float sdot = 0.0f;
+        if (doA) {
+          hasA = true;
+          for (int i = 0; i < D; i++) {
+            const float d = dIn_s[i];
+            sdot += d * phi[i];
+            A[i] += d * wp;
+          }
+        } else {
+          for (int i = 0; i < D; i++) sdot += dIn_s[i] * phi[i];
+        }
+        dX += sdot * gp;
+      }
+      __syncwarp();
+    }
+    if (act) dconf[s0 + lane] = dX;
+
+    // dW += E_g (x) phi_g over grid points with an E contribution.
+    const uint32_t em = __ballot_sync(0xffffffffu, ((int)lane < V) && involved && wE != 0.0f);
+    __syncwarp();
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const int jj = (int)lane + 32 * h;
+      if (jj < D) {
+        uint32_t mm = em;
+        while (mm) {
+          const int gg = __ffs(mm) - 1;
+          mm &= mm - 1;
+          const float x = phi_s[gg * DS + jj];
+#pragma unroll
+          for (int o = 0; o < OMAX; o++) dWacc[h][o] += E_s[gg * OMAX + o] * x;
+        }
+      }
+    }
+
+    // Hash-table scatter of A (dz, dy, dx corner order as hashgrid.h:43-45).
+    if (__any_sync(0xffffffffu, hasA)) {
+      for (int l = 0; l < L; l++) {
+        const int res = __ldg(sc.res + l);
+        const bool hsh = __ldg(sc.do_hash + l) != 0;
+        int3 b;
+        float3 tt;
+        level_setup(pos, res, b, tt);
+        float a[F];
+#pragma unroll
+        for (int f = 0; f < F; f++) a[f] = hasA ? A[l * F + f] : 0.0f;
+#pragma unroll
+        for (int dz = 0; dz < 2; dz++)
+#pragma unroll
+          for (int dy = 0; dy < 2; dy++)
+#pragma unroll
+            for (int dx = 0; dx < 2; dx++) {
+              float cw = 1.0f;
+              cw *= dx == 1 ? tt.x : 1.0f - tt.x;
+              cw *= dy == 1 ? tt.y : 1.0f - tt.y;
+              cw *= dz == 1 ? tt.z : 1.0f - tt.z;
+              const int e = corner_entry(b.x + dx, b.y + dy, b.z + dz, res, hsh, p0, p1, p2, sc.T, sc.Tmask);
+              const bool on = hasA && e >= 0 && cw != 0.0f;
+              float v[F];
+#pragma unroll
+              for (int f = 0; f < F; f++) v[f] = a[f] * cw;
+              scatter_add<F>(dtable + (size_t)l * F, e, on, v, (size_t)L * F, lane);
+            }
+      }
+    }
+    __syncwarp();
+  }
+
+  // CTA reduction of dW and db, then one global atomic per element.
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+    const int jj = (int)lane + 32 * h;
+    if (jj < D) {
+#pragma unroll
+      for (int o = 0; o < OMAX; o++)
+        if (o < O && dWacc[h][o] != 0.0f) atomicAdd(&dW_s[o * D + jj], dWacc[h][o]);
+    }
+  }
+  if ((int)lane < O && dbacc != 0.0f) atomicAdd(&db_s[lane], dbacc);
+  __syncthreads();
+  for (int i = threadIdx.x; i < O * D; i += blockDim.x)
+    if (dW_s[i] != 0.0f) atomicAdd(&dW[i], dW_s[i]);
+  for (int i = threadIdx.x; i < O; i += blockDim.x)
+    if (db_s[i] != 0.0f) atomicAdd(&db[i], db_s[i]);
+}
+
+template <int F, int OMAX>
+void launch_prim_t(const Scene& sc, GeomState& g, float* dconf, float* dtable, float* dW, float* db, cudaStream_t s) {
+  const int D = sc.L * F;
+  size_t smem = sizeof(float) * (2 * OMAX * D + OMAX + kBwdWarps * (2 * 32 * (D + 1) + 32 * OMAX + 64));
+  auto k = backward_prim_kernel<F, OMAX>;
+  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  int blocks = (sc.P + kBwdWarps - 1) / kBwdWarps;
+  blocks = blocks < 148 * 16 ? blocks : 148 * 16;
+  if (blocks < 1) blocks = 1;
+  k<<<blocks, kBwdWarps * 32, smem, s>>>(sc, g, dconf, dtable, dW, db);
+}
+
+}  // namespace
+
+void launch_backward(const Scene& sc, GeomState& g, const ImgState& im, const float* dL_dcolor, const float* dL_dfeat,
+                     float* dconf, float* dtable, float* dW, float* db, cudaStream_t s) {
+  const size_t N = (size_t)sc.W * sc.H;
+  cudaMemsetAsync(g.rec_flag, 0, (size_t)sc.P * sc.V, s);
+  const bool o16 = sc.O > 8;
+  if (N > 0) {
+    const unsigned blocks = (unsigned)((N + 255) / 256);
+    if (o16)
+      backward_pixel_kernel<16><<<blocks, 256, 0, s>>>(sc, g, im, dL_dcolor, dL_dfeat);
+    else
+      backward_pixel_kernel<8><<<blocks, 256, 0, s>>>(sc, g, im, dL_dcolor, dL_dfeat);
+  }
+  switch (sc.F) {
+    case 1: o16 ? launch_prim_t<1, 16>(sc, g, dconf, dtable, dW, db, s) : launch_prim_t<1, 8>(sc, g, dconf, dtable, dW, db, s); break;
+    case 2: o16 ? launch_prim_t<2, 16>(sc, g, dconf, dtable, dW, db, s) : launch_prim_t<2, 8>(sc, g, dconf, dtable, dW, db, s); break;
+    case 4: o16 ? launch_prim_t<4, 16>(sc, g, dconf, dtable, dW, db, s) : launch_prim_t<4, 8>(sc, g, dconf, dtable, dW, db, s); break;
+    case 8: o16 ? launch_prim_t<8, 16>(sc, g, dconf, dtable, dW, db, s) : launch_prim_t<8, 8>(sc, g, dconf, dtable, dW, db, s); break;
+    default: break;
+  }
+}
+
+}  // namespace vi

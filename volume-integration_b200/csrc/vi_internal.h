@@ -1,0 +1,118 @@
+// Internal (non-exported) declarations shared by the renderer's translation units:
+// the private layouts of the three state buffers and the kernel launchers.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace vi {
+
+constexpr int kSortThreads = 256;
+constexpr int kRadix = 256;
+
+inline size_t align_up(size_t x, size_t a = 256) { return (x + a - 1) / a * a; }
+
+// Scratch of one onesweep sort (see vi_sort.cu).
+struct SortTemp {
+  uint32_t* hist = nullptr;      // passes x 256 digit counts, then exclusive starts
+  uint32_t* lookback = nullptr;  // passes x tiles x 256 status words
+  uint32_t* counters = nullptr;  // passes tile counters
+  int passes = 0;
+  uint32_t tiles = 0;
+};
+size_t sort_temp_bytes(uint64_t n, int key_bytes, int begin_bit, int end_bit);
+void sort_temp_carve(char* base, uint64_t n, int key_bytes, int begin_bit, int end_bit, SortTemp& t);
+
+// Stable LSD radix sort of (key, value) pairs over bits [begin_bit, end_bit).
+// keys/vals hold the input; alt_* are same-sized scratch.  Returns true when the
+// sorted result ended up in alt_*, false when it is in keys/vals.
+bool onesweep_sort_u32(uint32_t* keys, uint32_t* vals, uint32_t* alt_keys, uint32_t* alt_vals, uint64_t n,
+                       int begin_bit, int end_bit, const SortTemp& t, uint32_t* status, cudaStream_t s);
+bool onesweep_sort_u64(uint64_t* keys, uint32_t* vals, uint64_t* alt_keys, uint32_t* alt_vals, uint64_t n,
+                       int begin_bit, int end_bit, const SortTemp& t, uint32_t* status, cudaStream_t s);
+
+// ---------------------------------------------------------------------------
+// Geometry state: everything sized by the primitive count P.
+// ---------------------------------------------------------------------------
+struct GeomState {
+  uint32_t* status;          // [0] status bits, [2..3] num_rendered as u64
+  float* depths;             // [P] view-space z of the centre
+  int* radii;                // [P]
+  float* means2D;            // [2P]
+  uint32_t* tiles_touched;   // [P]
+  uint32_t* dkeys;           // [P] depth sort keys (float bits, invisible = ~0)
+  uint32_t* didx;            // [P] primitive index, sorted along with dkeys
+  uint32_t* dkeys_alt;       // [P]
+  uint32_t* didx_alt;        // [P]
+  uint32_t* offsets;         // [P] exclusive overlap offsets in depth order
+  uint32_t* block_sums;      // [scan blocks]
+  uint32_t* rec_cnt;         // [P] record count | kBwdDiffers
+  uint32_t* rec_key;         // [P*V] tile*256 + pixel-in-tile, sorted per primitive
+  float* rec_props;          // [P*V*O] activated colour, features, density per record
+  uint8_t* rec_flag;         // [P*V] record is a contributor (written by the backward)
+  float* rec_dpre;           // [P*V*O] dL/d(pre-activation) per contributing record
+  SortTemp sort;
+  size_t bytes;
+};
+constexpr uint32_t kBwdDiffers = 0x80000000u;
+constexpr int kScanBlock = 2048;
+GeomState geom_layout(char* base, size_t P, int V, int O);
+
+// Binning state: everything sized by the overlap count R.
+struct BinState {
+  uint32_t* tkeys;      // [R] tile ids
+  uint32_t* tvals;      // [R] primitive ids
+  uint32_t* tkeys_alt;  // [R]
+  uint32_t* tvals_alt;  // [R]
+  SortTemp sort;
+  size_t bytes;
+};
+BinState bin_layout(char* base, uint64_t R, int tile_bits);
+
+// Image state: everything sized by the pixel count N.
+struct ImgState {
+  uint32_t* ranges;       // [2*tiles]
+  float* final_T;         // [N]
+  int32_t* n_contrib;     // [N]
+  int32_t* contrib_idx;   // [N*K] index into the sorted overlap list
+  float* delta_t;         // [N*K]
+  uint32_t* contrib_rec;  // [N*K] record slot of the contribution
+  size_t bytes;
+};
+ImgState img_layout(char* base, size_t N, int K, size_t tiles);
+
+// ---------------------------------------------------------------------------
+// Per-call constants.
+// ---------------------------------------------------------------------------
+struct Scene {
+  int P, W, H, G, V, D, O, L, F, Fout, K, genus;
+  uint32_t T, Tmask;
+  float scale, step, gof, near_plane, max_distance, focal_x, focal_y;
+  const float* means;
+  const float* conf;
+  const float* view;
+  const float* proj;
+  const float* table;
+  const int* res;
+  const int* do_hash;
+  const int* primes;
+  const float* Wl;
+  const float* bl;
+  const float* bg;
+  uint64_t table_numel;
+  unsigned gx, gy;
+};
+
+void launch_preprocess(const Scene& sc, GeomState& g, cudaStream_t s);
+void launch_offsets_scan(const Scene& sc, GeomState& g, const uint32_t* sorted_idx, cudaStream_t s);
+void launch_duplicate(const Scene& sc, const GeomState& g, const uint32_t* sorted_idx, BinState& b,
+                      cudaStream_t s);
+void launch_ranges(uint64_t R, const uint32_t* sorted_tiles, uint32_t* ranges, size_t tiles, cudaStream_t s);
+void launch_mark_visible(int P, const float* means, const float* view, bool* present, cudaStream_t s);
+void launch_features(const Scene& sc, GeomState& g, cudaStream_t s);
+void launch_render(const Scene& sc, const GeomState& g, const uint32_t* point_list, ImgState& im,
+                   float* out_color, float* out_feat, float* vis, cudaStream_t s);
+void launch_backward(const Scene& sc, GeomState& g, const ImgState& im, const float* dL_dcolor,
+                     const float* dL_dfeat, float* dconf, float* dtable, float* dW, float* db, cudaStream_t s);
+
+}  // namespace vi

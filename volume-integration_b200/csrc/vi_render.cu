@@ -1,0 +1,173 @@
+// Per-tile compositing: the per-pixel part of the reference render kernel
+// (forward.cu:467-785) over the records written by the feature stage.
+//
+// One CTA per 16x16 tile, one thread per pixel.  The tile's sorted list is
+// walked in batches of 64 entries.  For each batch the CTA locates every
+// entry's records inside this tile (they are contiguous: records are sorted by
+// tile) and marks, per pixel, a 64-bit mask of the entries that have a record
+// for it.  Each pixel then visits its set bits in list order and runs the
+// reference's pending-primitive compositing, so a pixel touches only the
+// primitives that actually cover it.  A __syncthreads_count at the top of each
+// batch ends the tile once every pixel is done (forward.cu:369-372).
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "vi_kernels.cuh"
+
+namespace vi {
+namespace {
+
+constexpr int kBatch = 64;
+
+template <int OMAX>
+__global__ void __launch_bounds__(VI_TILE_PIX) render_kernel(Scene sc, const uint32_t* __restrict__ point_list,
+                                                            const uint32_t* __restrict__ ranges,
+                                                            const float* __restrict__ depths,
+                                                            const uint32_t* __restrict__ rec_cnt,
+                                                            const uint32_t* __restrict__ rec_key,
+                                                            const float* __restrict__ rec_props,
+                                                            float* __restrict__ out_color, float* __restrict__ out_feat,
+                                                            float* __restrict__ vis, float* __restrict__ final_T,
+                                                            int32_t* __restrict__ n_contrib,
+                                                            int32_t* __restrict__ contrib_idx,
+                                                            float* __restrict__ delta_t,
+                                                            uint32_t* __restrict__ contrib_rec) {
+  __shared__ unsigned long long mask[VI_TILE_PIX];
+  __shared__ uint8_t slot[VI_TILE_PIX * kBatch];
+  __shared__ uint32_t ent_rec[kBatch];
+  __shared__ uint32_t ent_len[kBatch];
+  __shared__ float ent_depth[kBatch];
+
+  const int tid = threadIdx.x;
+  const unsigned tile = blockIdx.x;
+  const unsigned bx = tile % sc.gx, by = tile / sc.gx;
+  const unsigned px = bx * VI_TILE + (tid & 15), py = by * VI_TILE + (tid >> 4);
+  const bool inside = px < (unsigned)sc.W && py < (unsigned)sc.H;
+  const size_t pix = (size_t)py * sc.W + px;
+  const int O = sc.O, K = sc.K, Fout = sc.Fout, V = sc.V;
+
+  float T = 1.0f, C0 = 0.0f, C1 = 0.0f, C2 = 0.0f;
+  float Fe[OMAX - 4];
+#pragma unroll
+  for (int f = 0; f < OMAX - 4; f++) Fe[f] = 0.0f;
+  int cnt = 0;
+  bool done = !inside, has_p = false;
+  uint32_t pend_rec = 0, pend_gidx = 0;
+  float pend_depth = sc.near_plane, T_pend = 0.0f;
+
+  const uint32_t r0 = ranges[2 * tile], r1 = ranges[2 * tile + 1];
+  const uint32_t klo = tile << 8;
+
+  auto composite = [&](float dt) {
+    const float* pp = rec_props + (size_t)pend_rec * OMAX;
+    float alpha = 1.0f - expf(-pp[O - 1] * dt);
+    alpha = fminf(fmaxf(alpha, 0.0f), 1.0f);
+    const float wgt = T_pend * alpha;
+    C0 += wgt * pp[0];
+    C1 += wgt * pp[1];
+    C2 += wgt * pp[2];
+#pragma unroll
+    for (int f = 0; f < OMAX - 4; f++)
+      if (f < Fout) Fe[f] += wgt * pp[3 + f];
+    T = T_pend * (1.0f - alpha);
+    const size_t w = pix * K + cnt;
+    contrib_idx[w] = (int32_t)pend_gidx;
+    delta_t[w] = dt;
+    contrib_rec[w] = pend_rec;
+    cnt++;
+  };
+
+  for (uint32_t base = r0; base < r1; base += kBatch) {
+    if (__syncthreads_count(!done) == 0) break;
+    const int nb = (int)min((uint32_t)kBatch, r1 - base);
+    if (tid < nb) {
+      const uint32_t q = point_list[base + tid];
+      const uint32_t n = rec_cnt[q] & ~kBwdDiffers;
+      const uint32_t* keys = rec_key + (size_t)q * V;
+      uint32_t lo = 0, hi = n;  // first record with key >= klo
+      while (lo < hi) {
+        uint32_t mid = (lo + hi) >> 1;
+        if (keys[mid] < klo) lo = mid + 1; else hi = mid;
+      }
+      uint32_t e = lo;
+      while (e < n && keys[e] < klo + 256u) e++;
+      ent_rec[tid] = (uint32_t)((size_t)q * V + lo);
+      ent_len[tid] = e - lo;
+      ent_depth[tid] = depths[q];
+    }
+    mask[tid] = 0ull;
+    __syncthreads();
+    // Warp w scatters the records of entries w, w+8, ...
+    {
+      const int w = tid >> 5, lane = tid & 31;
+      for (int e = w; e < nb; e += VI_TILE_PIX / 32) {
+        const uint32_t len = ent_len[e];
+        if ((uint32_t)lane < len) {
+          const uint32_t lp = rec_key[ent_rec[e] + lane] & 255u;
+          slot[lp * kBatch + e] = (uint8_t)lane;
+          atomicOr(&mask[lp], 1ull << e);
+        }
+      }
+    }
+    __syncthreads();
+    if (!done) {
+      unsigned long long m = mask[tid];
+      while (m) {
+        const int e = __ffsll(m) - 1;
+        m &= m - 1;
+        const uint32_t rec = ent_rec[e] + slot[tid * kBatch + e];
+        const float depth = ent_depth[e];
+        if (has_p) {
+          const float dt = fmaxf(0.0f, depth - pend_depth);
+          if (dt > 1e-5f && cnt < K) composite(dt);
+        }
+        if (T >= 1e-4f && cnt < K) {
+          pend_rec = rec;
+          pend_depth = depth;
+          pend_gidx = base + e;
+          has_p = true;
+          T_pend = T;
+        } else {
+          has_p = false;
+          done = true;
+        }
+        if (T < 1e-4f || cnt >= K) done = true;
+        if (done) break;
+      }
+    }
+  }
+  if (!inside) return;
+  if (has_p && T >= 1e-4f && cnt < K) {
+    const float dt = fmaxf(0.0f, sc.max_distance - pend_depth);
+    if (dt > 1e-5f) composite(dt);
+  }
+  const size_t N = (size_t)sc.W * sc.H;
+  out_color[pix] = fminf(fmaxf(C0 + T * sc.bg[0], 0.0f), 1.0f);
+  out_color[N + pix] = fminf(fmaxf(C1 + T * sc.bg[1], 0.0f), 1.0f);
+  out_color[2 * N + pix] = fminf(fmaxf(C2 + T * sc.bg[2], 0.0f), 1.0f);
+#pragma unroll
+  for (int f = 0; f < OMAX - 4; f++)
+    if (f < Fout) out_feat[f * N + pix] = Fe[f];
+  vis[pix] = 1.0f - T;
+  final_T[pix] = T;
+  n_contrib[pix] = cnt;
+}
+
+}  // namespace
+
+void launch_render(const Scene& sc, const GeomState& g, const uint32_t* point_list, ImgState& im, float* out_color,
+                   float* out_feat, float* vis, cudaStream_t s) {
+  const unsigned tiles = sc.gx * sc.gy;
+  if (tiles == 0) return;
+  if (sc.O > 8)
+    render_kernel<16><<<tiles, VI_TILE_PIX, 0, s>>>(sc, point_list, im.ranges, g.depths, g.rec_cnt, g.rec_key,
+                                                    g.rec_props, out_color, out_feat, vis, im.final_T, im.n_contrib,
+                                                    im.contrib_idx, im.delta_t, im.contrib_rec);
+  else
+    render_kernel<8><<<tiles, VI_TILE_PIX, 0, s>>>(sc, point_list, im.ranges, g.depths, g.rec_cnt, g.rec_key,
+                                                   g.rec_props, out_color, out_feat, vis, im.final_T, im.n_contrib,
+                                                   im.contrib_idx, im.delta_t, im.contrib_rec);
+}
+
+}  // namespace vi
