@@ -1,0 +1,420 @@
+#!/usr/bin/env python
+"""Forward+backward frames/s of the volume-integration renderer on B200.
+
+A step is one forward + backward of one 1920x1080 view of the 1M-primitive
+scene with a 16-level hashgrid (the headline workload), through the drop-in
+autograd Function, with dL/dimage ~ N(0,1) fixed per run.  Under torchrun each
+rank renders its own view of the same scene (cameras on an orbit: weak
+scaling, views sharded across GPUs) and the gradients are summed over ranks
+with one NCCL all-reduce per step.
+
+Prints one JSON line (rank 0).  `--impl reference` times the CPU restatement
+of the reference algorithm on the host cores instead (there is no reference
+CPU implementation; its CUDA extension is not run).
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (os.path.join(ROOT, "volume-integration_b200"), os.path.join(ROOT, "oracle"), os.path.join(ROOT, "tests")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "fwd+bwd frames/s at 1080p, 1M Gaussians + 16-lvl hashgrid; sort Gkeys/s"
+STAGES = ["preprocess", "depth_sort", "offsets", "features", "binning", "render", "bwd_pixel", "bwd_prim"]
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="headline")
+    ap.add_argument("--cpu-seconds", type=float, default=20.0, help="budget of the CPU baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# workload
+# ---------------------------------------------------------------------------
+def workload(config, rank, world, device):
+    import vi_workloads as wl
+    import vi_testlib as tl
+    means, conf, kw, cams = wl.make(config)
+    c = wl.CONFIGS[config]
+    if world > 1 and len(cams) < world:
+        cams = wl.orbit(world, c["dist"], c["width"], c["height"], c["fov"])
+    cam = cams[rank % len(cams)]
+    s = tl.settings_from(kw, cam, device)
+    gen = torch.Generator().manual_seed(77 + rank)
+    dc = torch.randn(3, s.image_height, s.image_width, generator=gen).to(device)
+    df = torch.randn(s.output_feature_dim, s.image_height, s.image_width, generator=gen).to(device)
+    return means.to(device), conf.to(device), s, dc, df
+
+
+def algorithmic_bytes(st, s, P):
+    """Compulsory bytes per stage (fixed formulas, independent of the implementation)."""
+    V = s.grid_size ** 3
+    L, F, T = s.hashgrid_levels, s.input_feature_dim, s.feature_offset
+    D, Fout = L * F, s.output_feature_dim
+    O = 3 + Fout + 1
+    N = s.image_height * s.image_width
+    tiles = ((s.image_width + 15) // 16) * ((s.image_height + 15) // 16)
+    R, Pv, Kt = st["R"], st["Pv"], st["Kt"]
+    from volume_integration import _C
+    passes = math.ceil(_C.sort_end_bit(tiles) / 8)
+    return {
+        "preprocess": 12 * P + 20 * P,
+        "sort": 8 * P + 20 * P + 12 * R + 24 * R * passes + 8 * R + 8 * tiles,
+        "features": Pv * (12 + 4 * V) + 4 * T * L * F + 4 * Pv * V * (O + 2),
+        "render": R * (4 + 4 * V * (O + 3)) + 8 * tiles + 4 * N * (3 + Fout + 3) + 8 * Kt,
+        "backward": 4 * N * (3 + Fout) + 12 * N + 8 * Kt + R * (4 + 4 * V * (O + 3)) + 4 * T * L * F * 2
+                    + 4 * P * V + 4 * (D * O + O),
+    }
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class Clocks:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.proc = None
+        try:
+            bus = torch.cuda.get_device_properties(device).pci_bus_id
+            sel = ["--id=" + bus]
+        except Exception:
+            sel = ["-i", str(device)]
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits",
+                                          "-lms", "200"] + sel, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                                         text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out = ""
+        rows = []
+        for line in out.strip().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) != 7:
+                continue
+            try:
+                rows.append((float(parts[0]), float(parts[1]), parts[3:]))
+            except ValueError:
+                continue
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(args):
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    device = torch.device("cuda", torch.cuda.current_device())
+    import volume_integration as vi
+    from volume_integration import _C
+
+    means, conf, s, dc, df = workload(args.config, rank, world, device)
+    P = means.shape[0]
+    confp = conf.clone().requires_grad_(True)
+    table = s.feature_table.clone().requires_grad_(True)
+    Wl = s.linear_weights.clone().requires_grad_(True)
+    bl = s.linear_bias.clone().requires_grad_(True)
+    leaves = [confp, table, Wl, bl]
+
+    def step(m, c, t, w, b):
+        oc, of, vis = vi.integrate_primitives(m, c, t, w, b, s)
+        grads = torch.autograd.grad([oc, of], [c, t, w, b], [dc, df])
+        if world > 1:
+            works = [dist.all_reduce(g, async_op=True) for g in grads]
+            for wk in works:
+                wk.wait()
+        return oc, of, vis, grads
+
+    # workload statistics for the roofline (one forward, outside timing)
+    from vi_testlib import gpu_state
+    st = gpu_state(means, conf, s)
+    stats = {"R": int(st["num_rendered"]), "Pv": int((st["radii"] > 0).sum()), "Kt": int(st["n_contrib"].sum())}
+    del st
+
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)  # > 126 MB L2
+    for _ in range(args.warmup):
+        step(means, *leaves)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
+    _C.profile_read(True)
+    _C.profile_enable(True)
+    launches0 = _C.kernel_launches()
+    clocks = Clocks(device.index)
+    times = []
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        flush.zero_()
+        ev[i][0].record()
+        step(means, *leaves)
+        ev[i][1].record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    launches = _C.kernel_launches() - launches0
+    _C.profile_enable(False)
+    prof = _C.profile_read(True)
+    times = [a.elapsed_time(b) for a, b in ev]
+    total_ms = sum(times)
+    if world > 1:
+        t = torch.tensor([total_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+        dist.barrier()
+    value = world * args.steps / (total_ms / 1000.0)
+
+    # roofline of the dominant stage, timed live on the launching stream
+    peak, peak_kind = measured_peaks()
+    ab = algorithmic_bytes(stats, s, P)
+    stage_ms = {k: v[0] for k, v in prof.items()}
+    stage_calls = {k: v[1] for k, v in prof.items()}
+    groups = {"features": ["features"], "render": ["render"], "backward": ["bwd_pixel", "bwd_prim"],
+              "sort": ["depth_sort", "offsets", "binning"], "preprocess": ["preprocess"]}
+    gms = {g: sum(stage_ms[k] for k in ks) for g, ks in groups.items()}
+    dom = max(gms, key=gms.get)
+    per_launch_ms = gms[dom] / max(1, args.steps)
+    achieved = ab[dom] / (per_launch_ms / 1000.0) / 1e9
+    roofline = {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
+                "algorithmic_bytes": int(ab[dom]), "ms_per_launch": round(per_launch_ms, 4)}
+    sort_ms = gms["sort"] / max(1, args.steps)
+    sort_gkeys = stats["R"] / (sort_ms / 1000.0) / 1e9 if sort_ms > 0 else None
+
+    line = {"metric": METRIC, "value": round(value, 3), "unit": "frames/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"{args.config}: {P} primitives, {s.image_width}x{s.image_height}, "
+                                   f"L={s.hashgrid_levels} F={s.input_feature_dim} T=2^{int(math.log2(s.feature_offset))}"
+                                   f", G={s.grid_size}, K={s.max_primitives_per_ray}, one view per GPU",
+                       "global_batch": world, "parallelism": f"views sharded dp{world}",
+                       "l2": "256 MB buffer written between timed steps",
+                       "num_rendered": stats["R"], "visible_primitives": stats["Pv"],
+                       "contributions": stats["Kt"]},
+            "roofline": roofline,
+            "stage_ms_per_step": {k: round(v / max(1, args.steps), 4) for k, v in stage_ms.items()},
+            "sort_gkeys_per_s": round(sort_gkeys, 3) if sort_gkeys else None,
+            "gpu_launches": int(launches), "gpu_launches_per_step": round(launches / args.steps, 2),
+            "clocks": clk}
+
+    if not args.no_e2e:
+        line["e2e"] = run_e2e(args, vi, means, conf, s, dc, df, world, dist if world > 1 else None, device)
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(args.config, args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+
+
+def run_e2e(args, vi, means, conf, s, dc, df, world, dist, device):
+    """Same step through the public API with host inputs: pinned H2D copies of every
+    input and D2H copies of the images and gradients inside the timed region."""
+    host_in = [t.detach().cpu().pin_memory() for t in (means, conf, s.feature_table, s.linear_weights,
+                                                      s.linear_bias, dc, df)]
+    dev_in = [torch.empty_like(t, device=device) for t in host_in]
+    outs = None
+    h2d = sum(t.numel() * t.element_size() for t in host_in)
+
+    def one():
+        nonlocal outs
+        for d, h in zip(dev_in, host_in):
+            d.copy_(h, non_blocking=True)
+        m, c, t, w, b, gc, gf = dev_in
+        c.requires_grad_(True)
+        t.requires_grad_(True)
+        w.requires_grad_(True)
+        b.requires_grad_(True)
+        oc, of, vis = vi.integrate_primitives(m, c, t, w, b, s)
+        grads = torch.autograd.grad([oc, of], [c, t, w, b], [gc, gf])
+        if dist is not None:
+            for g in grads:
+                dist.all_reduce(g)
+        res = [oc.detach(), of.detach(), vis.detach()] + list(grads)
+        if outs is None:
+            outs = [torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res]
+        for o, r in zip(outs, res):
+            o.copy_(r, non_blocking=True)
+        for d in dev_in:
+            d.requires_grad_(False)
+
+    for _ in range(max(1, args.warmup)):
+        one()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        one()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b)
+    if dist is not None:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    d2h = sum(o.numel() * o.element_size() for o in outs)
+    return {"value": round(world * args.steps / (ms / 1000.0), 3), "unit": "frames/s",
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)}
+
+
+# ---------------------------------------------------------------------------
+# CPU restatement (the reported baseline and the reference arm)
+# ---------------------------------------------------------------------------
+_CPU_SCENES = {}
+
+
+def cpu_scene(config):
+    import oracle as orc
+    import vi_workloads as wl
+    if config in _CPU_SCENES:
+        return _CPU_SCENES[config]
+    means, conf, kw, cams = wl.make(config)
+    cam = cams[0]
+    sc = orc.Scene(means.numpy(), conf.numpy(), kw["primitive_scale"], cam["viewmatrix"].numpy(),
+                   cam["projmatrix"].numpy(), cam["tanfovx"], cam["tanfovy"], cam["image_height"],
+                   cam["image_width"], kw["near_plane"], kw["max_distance"], kw["feature_table"].numpy(),
+                   kw["resolution"].numpy(), kw["do_hash"].numpy(), kw["primes"].numpy(), kw["feature_offset"],
+                   kw["linear_weights"].numpy(), kw["linear_bias"].numpy(), kw["stencil_genus"], kw["grid_size"],
+                   kw["max_primitives_per_ray"], kw["bg_color"].numpy(), kw["input_feature_dim"],
+                   kw["output_feature_dim"], kw["hashgrid_levels"])
+    gen = np.random.default_rng(5)
+    dc = gen.standard_normal((3, sc.H, sc.W)).astype(np.float32)
+    dfe = gen.standard_normal((sc.Fout, sc.H, sc.W)).astype(np.float32)
+    _CPU_SCENES[config] = (sc, dc, dfe)
+    return _CPU_SCENES[config]
+
+
+def cpu_frame_sample(config, budget_s, threads):
+    """Times the oracle on a bounded sample of one frame: the full preprocess and
+    binning, then render + backward on every k-th tile, extrapolated to all
+    tiles.  Returns (frames/s, description)."""
+    import oracle as orc
+    sc, dc, dfe = cpu_scene(config)
+    t0 = time.perf_counter()
+    pre = orc.preprocess(sc)
+    b = orc.binning(sc, pre)
+    t_bin = time.perf_counter() - t0
+    tiles = sc.tiles
+    # calibrate on a small sample, then size the main sample to the budget
+    k = 257
+    mask = np.zeros(tiles, np.uint8)
+    mask[::k] = 1
+    t0 = time.perf_counter()
+    f = orc.render(sc, b, tile_mask=mask, threads=threads)
+    f.update(b)
+    orc.backward(sc, b, f, dc, dfe, tile_mask=mask, threads=threads)
+    t_cal = time.perf_counter() - t0
+    per_tile = t_cal / max(1, int(mask.sum()))
+    want = max(1, int(max(1.0, budget_s - t_bin) / max(per_tile, 1e-6)))
+    k = max(1, tiles // want)
+    mask = np.zeros(tiles, np.uint8)
+    mask[::k] = 1
+    t0 = time.perf_counter()
+    f = orc.render(sc, b, tile_mask=mask, threads=threads)
+    f.update(b)
+    orc.backward(sc, b, f, dc, dfe, tile_mask=mask, threads=threads)
+    t_smp = time.perf_counter() - t0
+    n = int(mask.sum())
+    frame_s = t_bin + t_smp * tiles / n
+    desc = (f"{config}: full preprocess + binning ({t_bin:.2f} s), render+backward on every {k}-th tile "
+            f"({n}/{tiles} tiles, {t_smp:.2f} s) extrapolated to the frame; {threads} threads")
+    return 1.0 / frame_s, desc
+
+
+def cpu_baseline(config, budget_s):
+    threads = os.cpu_count() or 1
+    v, desc = cpu_frame_sample(config, budget_s, threads)
+    return {"value": round(v, 5), "unit": "frames/s", "cores": threads, "kind": "port", "sample": desc}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    budget = max(2.0, min(10.0, 150.0 / max(1, args.steps + args.warmup)))
+    for _ in range(args.warmup):
+        cpu_frame_sample(args.config, budget, threads)
+    vals, descs = [], []
+    for _ in range(args.steps):
+        v, d = cpu_frame_sample(args.config, budget, threads)
+        vals.append(v)
+        descs.append(d)
+    value = len(vals) / sum(1.0 / v for v in vals)
+    line = {"metric": METRIC, "value": round(value, 5), "unit": "frames/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000.0 / value, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": f"{args.config} (same scene and camera as the GPU arm)"},
+            "cpu_baseline": {"value": round(value, 5), "unit": "frames/s", "cores": threads, "kind": "port",
+                             "sample": descs[-1]},
+            "e2e": {"value": round(value, 5), "unit": "frames/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -131,6 +131,19 @@ int vi_get_state_layout(int P, int64_t num_rendered, int image_height, int image
 /* Reads the status word a forward latched in its geometry buffer (blocks). */
 int vi_read_device_status(const char* geom_buffer, uint32_t* status, void* stream);
 
+/* Kernels launched by this library so far (all threads, all devices). */
+uint64_t vi_kernel_launches(void);
+
+/*
+ * Per-stage timing with CUDA events on the launching stream (off by default).
+ * Stages, in order: 0 preprocess, 1 depth sort, 2 overlap offsets, 3 feature
+ * stage, 4 binning (duplicate + tile sort + ranges), 5 render, 6 backward
+ * per-pixel, 7 backward per-primitive.  vi_profile_read waits for the recorded
+ * events and returns the summed milliseconds and call counts per stage.
+ */
+int vi_profile_enable(int on);
+int vi_profile_read(double* ms, uint64_t* calls, int n, int reset);
+
 #ifdef __cplusplus
 }
 #endif

@@ -26,6 +26,12 @@ Tensor cuda_f32(const Tensor& t, const char* name) {
   TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
   return t.to(torch::kFloat32).contiguous();
 }
+// The kernels load one table entry's features as one vector: realign views with an odd offset.
+Tensor aligned_table(const Tensor& t) {
+  Tensor c = cuda_f32(t, "feature_table");
+  if (reinterpret_cast<uintptr_t>(c.data_ptr()) % 16 != 0) c = c.clone();
+  return c;
+}
 Tensor cuda_i32(const Tensor& t, const char* name) {
   TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
   return t.to(torch::kInt32).contiguous();
@@ -47,7 +53,7 @@ std::tuple<int, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor> integrate_primit
   const int P = (int)means3D.size(0), H = (int)image_height, W = (int)image_width;
   Tensor m = cuda_f32(means3D, "means3D"), c = cuda_f32(primitive_confidences, "primitive_confidences");
   Tensor vm = cuda_f32(viewmatrix, "viewmatrix"), pm = cuda_f32(projmatrix, "projmatrix");
-  Tensor cp = cuda_f32(cam_pos, "cam_pos"), ft = cuda_f32(feature_table, "feature_table");
+  Tensor cp = cuda_f32(cam_pos, "cam_pos"), ft = aligned_table(feature_table);
   Tensor rs = cuda_i32(resolution, "resolution"), dh = cuda_i32(do_hash, "do_hash"), pr = cuda_i32(primes, "primes");
   Tensor lw = cuda_f32(linear_weights, "linear_weights"), lb = cuda_f32(linear_bias, "linear_bias");
   Tensor bg = cuda_f32(bg_color, "bg_color");
@@ -91,7 +97,7 @@ std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> integrate_primitives_backward
   const at::cuda::CUDAGuard guard(means3D.device());
   Tensor m = cuda_f32(means3D, "means3D"), c = cuda_f32(primitive_confidences, "primitive_confidences");
   Tensor vm = cuda_f32(viewmatrix, "viewmatrix"), pm = cuda_f32(projmatrix, "projmatrix");
-  Tensor cp = cuda_f32(cam_pos, "cam_pos"), ft = cuda_f32(feature_table, "feature_table");
+  Tensor cp = cuda_f32(cam_pos, "cam_pos"), ft = aligned_table(feature_table);
   Tensor rs = cuda_i32(resolution, "resolution"), dh = cuda_i32(do_hash, "do_hash"), pr = cuda_i32(primes, "primes");
   Tensor lw = cuda_f32(linear_weights, "linear_weights"), lb = cuda_f32(linear_bias, "linear_bias");
   Tensor bg = cuda_f32(bg_color, "bg_color");
@@ -99,6 +105,9 @@ std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> integrate_primitives_backward
   Tensor gf = dL_dout_features.numel() ? cuda_f32(dL_dout_features, "dL_dout_features") : dL_dout_features;
   TORCH_CHECK(gc.numel() == 3 * image_height * image_width, "dL_dout_color must be (3, H, W)");
   TORCH_CHECK(gf.numel() == output_feature_dim * image_height * image_width, "dL_dout_features must be (F_out, H, W)");
+  const int64_t D = hashgrid_levels * input_feature_dim, O = num_output_channels + output_feature_dim + 1;
+  TORCH_CHECK(lw.numel() >= O * D && lb.numel() >= O, "linear layer needs ", O * D, " weights and ", O, " biases");
+  TORCH_CHECK(c.numel() == P * grid_size * grid_size * grid_size, "primitive_confidences must be (P, G^3)");
   Tensor dmeans = torch::empty_like(m), dconf = torch::empty_like(c), dtable = torch::empty_like(ft);
   Tensor dW = torch::empty_like(lw), db = torch::empty_like(lb);
   ok(vi_integrate_primitives_backward(
@@ -190,4 +199,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("state_views", &state_views, "Integer state of a forward call in the reference's formats");
   m.def("sort_pairs", &sort_pairs, "Stable radix sort of (uint64 key, uint32 value) pairs");
   m.def("sort_end_bit", [](int64_t tiles) { return vi_sort_end_bit((uint32_t)tiles); });
+  m.def("kernel_launches", []() { return (uint64_t)vi_kernel_launches(); });
+  m.def("profile_enable", [](bool on) { ok(vi_profile_enable(on ? 1 : 0)); });
+  m.def("profile_read", [](bool reset) {
+    double ms[8];
+    uint64_t calls[8];
+    ok(vi_profile_read(ms, calls, 8, reset ? 1 : 0));
+    static const char* names[8] = {"preprocess", "depth_sort", "offsets", "features",
+                                   "binning", "render", "bwd_pixel", "bwd_prim"};
+    py::dict d;
+    for (int i = 0; i < 8; i++) d[names[i]] = py::make_tuple(ms[i], calls[i]);
+    return d;
+  });
 }

@@ -3,7 +3,10 @@
 // cuda_integrator/integrator_impl.cu:196-469 and :474-756).
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdarg>
+#include <mutex>
+#include <vector>
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
@@ -67,7 +70,51 @@ cudaEvent_t event_for_device() {
   return g_events[dev];
 }
 
+std::atomic<unsigned long long> g_launch_count{0};
+
+// Stage timing: events recorded on the launching stream, resolved on read.
+struct StagePair {
+  int stage;
+  cudaEvent_t a, b;
+};
+std::mutex g_prof_mu;
+bool g_prof_on = false;
+std::vector<StagePair> g_prof_pending;
+std::vector<cudaEvent_t> g_prof_free;
+double g_prof_ms[kStCount] = {};
+unsigned long long g_prof_calls[kStCount] = {};
+thread_local cudaEvent_t g_open[kStCount] = {};
+
+cudaEvent_t prof_event() {
+  if (!g_prof_free.empty()) {
+    cudaEvent_t e = g_prof_free.back();
+    g_prof_free.pop_back();
+    return e;
+  }
+  cudaEvent_t e;
+  cudaEventCreate(&e);
+  return e;
+}
+
 }  // namespace
+
+void note_launches(int n) { g_launch_count.fetch_add((unsigned long long)n, std::memory_order_relaxed); }
+
+void stage_begin(Stage st, cudaStream_t s) {
+  if (!g_prof_on) return;
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  g_open[st] = prof_event();
+  cudaEventRecord(g_open[st], s);
+}
+
+void stage_end(Stage st, cudaStream_t s) {
+  if (!g_prof_on || !g_open[st]) return;
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  cudaEvent_t e = prof_event();
+  cudaEventRecord(e, s);
+  g_prof_pending.push_back({(int)st, g_open[st], e});
+  g_open[st] = nullptr;
+}
 
 GeomState geom_layout(char* base, size_t P, int V, int O) {
   GeomState g;
@@ -218,6 +265,9 @@ extern "C" int vi_integrate_primitives(
   if (feature_table_numel < (uint64_t)sc.T * sc.L * sc.F)
     return fail(VI_ERR_INVALID_ARGUMENT, "feature_table has %llu elements, needs feature_offset*L*F=%llu",
                 (unsigned long long)feature_table_numel, (unsigned long long)sc.T * sc.L * sc.F);
+  if (((uintptr_t)feature_table) % (size_t)(sc.F >= 4 ? 16 : sc.F * 4) != 0)
+    return fail(VI_ERR_INVALID_ARGUMENT, "feature_table must be aligned to %d bytes (vector loads of one entry)",
+                sc.F >= 4 ? 16 : sc.F * 4);
   if (linear_weights_numel < (uint64_t)sc.O * sc.D || linear_bias_numel < (uint64_t)sc.O)
     return fail(VI_ERR_INVALID_ARGUMENT, "linear layer needs %d weights and %d biases, got %llu and %llu",
                 sc.O * sc.D, sc.O, (unsigned long long)linear_weights_numel, (unsigned long long)linear_bias_numel);
@@ -236,20 +286,28 @@ extern "C" int vi_integrate_primitives(
   GeomState g = geom_layout(nullptr, P, sc.V, sc.O);
   char* gb = geom_buffer(geom_user, g.bytes);
   if (!gb) return fail(VI_ERR_ALLOC, "geometry buffer of %zu bytes", g.bytes);
+  if ((uintptr_t)gb & 255) return fail(VI_ERR_INVALID_ARGUMENT, "state buffers must be 256-byte aligned");
   g = geom_layout(gb, P, sc.V, sc.O);
   ImgState im = img_layout(nullptr, N, sc.K, tiles);
   char* ib = img_buffer(img_user, im.bytes);
   if (!ib) return fail(VI_ERR_ALLOC, "image buffer of %zu bytes", im.bytes);
+  if ((uintptr_t)ib & 255) return fail(VI_ERR_INVALID_ARGUMENT, "state buffers must be 256-byte aligned");
   im = img_layout(ib, N, sc.K, tiles);
 
   cudaMemsetAsync(g.status, 0, 64 * sizeof(uint32_t), s);
+  stage_begin(kStPreprocess, s);
   launch_preprocess(sc, g, s);
+  stage_end(kStPreprocess, s);
   if ((rc = check(s, debug, "preprocess", g.status))) return rc;
+  stage_begin(kStDepthSort, s);
   const bool depth_alt =
       onesweep_sort_u32(g.dkeys, g.didx, g.dkeys_alt, g.didx_alt, (uint64_t)P, 0, 32, g.sort, g.status, s);
+  stage_end(kStDepthSort, s);
   const uint32_t* sorted_idx = depth_alt ? g.didx_alt : g.didx;
   if ((rc = check(s, debug, "depth sort", g.status))) return rc;
+  stage_begin(kStOffsets, s);
   launch_offsets_scan(sc, g, sorted_idx, s);
+  stage_end(kStOffsets, s);
   if (!g_pinned) {
     cudaError_t e = cudaHostAlloc((void**)&g_pinned, 64, cudaHostAllocPortable);
     if (e != cudaSuccess) return cuda_fail(e, "pinned staging buffer");
@@ -259,7 +317,9 @@ extern "C" int vi_integrate_primitives(
   cudaEventRecord(ev, s);
   // The feature stage depends only on preprocess: queue it before blocking on
   // the overlap count so the GPU works while the host waits.
+  stage_begin(kStFeatures, s);
   launch_features(sc, g, s);
+  stage_end(kStFeatures, s);
   if ((rc = check(s, debug, "features", g.status))) return rc;
   cudaError_t e = cudaEventSynchronize(ev);
   if (e != cudaSuccess) return cuda_fail(e, "overlap count readback");
@@ -272,9 +332,11 @@ extern "C" int vi_integrate_primitives(
   BinState b = bin_layout(nullptr, R, tb);
   char* bb = binning_buffer(binning_user, b.bytes);
   if (!bb) return fail(VI_ERR_ALLOC, "binning buffer of %zu bytes", b.bytes);
+  if ((uintptr_t)bb & 255) return fail(VI_ERR_INVALID_ARGUMENT, "state buffers must be 256-byte aligned");
   b = bin_layout(bb, R, tb);
   const uint32_t* point_list = b.tvals;
   const uint32_t* sorted_tiles = b.tkeys;
+  stage_begin(kStBinning, s);
   if (R > 0) {
     launch_duplicate(sc, g, sorted_idx, b, s);
     if ((rc = check(s, debug, "duplicate", g.status))) return rc;
@@ -284,7 +346,10 @@ extern "C" int vi_integrate_primitives(
     if ((rc = check(s, debug, "tile sort", g.status))) return rc;
   }
   launch_ranges(R, sorted_tiles, im.ranges, tiles, s);
+  stage_end(kStBinning, s);
+  stage_begin(kStRender, s);
   launch_render(sc, g, point_list, im, out_color, out_features, visibility_info, s);
+  stage_end(kStRender, s);
   if ((rc = check(s, debug, "render", g.status))) return rc;
   *num_rendered = (int)R;
   return VI_OK;
@@ -325,6 +390,11 @@ extern "C" int vi_integrate_primitives_backward(
   const size_t N = (size_t)sc.W * sc.H;
   if (num_rendered <= 0 || P == 0 || N == 0) return check(s, debug, "empty backward", nullptr);
   if (!geom_buffer || !img_buffer) return fail(VI_ERR_INVALID_ARGUMENT, "forward state buffers are required");
+  if (((uintptr_t)geom_buffer & 255) || ((uintptr_t)img_buffer & 255))
+    return fail(VI_ERR_INVALID_ARGUMENT, "state buffers must be 256-byte aligned");
+  if (((uintptr_t)feature_table) % (size_t)(sc.F >= 4 ? 16 : sc.F * 4) != 0 ||
+      ((uintptr_t)dL_dfeature_table) % (size_t)(sc.F >= 4 ? 16 : sc.F * 4) != 0)
+    return fail(VI_ERR_INVALID_ARGUMENT, "feature_table and its gradient must be aligned to one entry's vector");
   GeomState g = geom_layout(geom_buffer, P, sc.V, sc.O);
   ImgState im = img_layout(img_buffer, N, sc.K, (size_t)sc.gx * sc.gy);
   launch_backward(sc, g, im, dL_dout_color, sc.Fout ? dL_dout_features : nullptr, dL_dconfidences,
@@ -405,4 +475,37 @@ extern "C" int vi_read_device_status(const char* geom_buffer, uint32_t* status, 
   cudaError_t e = cudaMemcpyAsync(status, g.status, 4, cudaMemcpyDeviceToHost, (cudaStream_t)stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
   return e == cudaSuccess ? VI_OK : cuda_fail(e, "read status");
+}
+
+extern "C" uint64_t vi_kernel_launches(void) { return g_launch_count.load(); }
+
+extern "C" int vi_profile_enable(int on) {
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  g_prof_on = on != 0;
+  return VI_OK;
+}
+
+extern "C" int vi_profile_read(double* ms, uint64_t* calls, int n, int reset) {
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  for (auto& p : g_prof_pending) {
+    cudaError_t e = cudaEventSynchronize(p.b);
+    if (e != cudaSuccess) return cuda_fail(e, "profile read");
+    float t = 0.0f;
+    cudaEventElapsedTime(&t, p.a, p.b);
+    g_prof_ms[p.stage] += t;
+    g_prof_calls[p.stage] += 1;
+    g_prof_free.push_back(p.a);
+    g_prof_free.push_back(p.b);
+  }
+  g_prof_pending.clear();
+  for (int i = 0; i < n && i < kStCount; i++) {
+    if (ms) ms[i] = g_prof_ms[i];
+    if (calls) calls[i] = g_prof_calls[i];
+  }
+  if (reset)
+    for (int i = 0; i < kStCount; i++) {
+      g_prof_ms[i] = 0.0;
+      g_prof_calls[i] = 0;
+    }
+  return VI_OK;
 }

@@ -61,7 +61,7 @@ __device__ void gather_generic(const Scene& sc, float3 pos, float* phi) {
 // Activated properties of primitive q seen from pixel (px, py) with the backward
 // projection 1/w (backward.cu:404-569).
 template <int OMAX>
-__device__ void recompute_props(const Scene& sc, uint32_t q, int px, int py, float* props) {
+__device__ __noinline__ void recompute_props(const Scene& sc, uint32_t q, int px, int py, float* props) {
   const int V = sc.V, G = sc.G, D = sc.D, O = sc.O;
   const Stencil st = make_stencil(sc.genus);
   float conf[32];
@@ -171,18 +171,15 @@ __global__ void __launch_bounds__(256) backward_pixel_kernel(Scene sc, GeomState
   }
 }
 
-// Sums F values over the lanes of each distinct table address, then one vector
-// atomic per address.  Falls back to plain per-lane atomics when addresses are
-// mostly distinct.
+// Adds v (F floats) at table slot e for every lane with `on`.  When every active
+// lane targets the same slot -- points clamped to the hashgrid box all land on one
+// corner cell -- the values are summed across the warp first and one vector
+// atomic is issued; otherwise each lane issues its own vector atomic.
 template <int F>
-__device__ __forceinline__ void scatter_add(float* __restrict__ dst_base, int e, bool act, const float* v, size_t stride,
+__device__ __forceinline__ void scatter_add(float* __restrict__ dst_base, int e, bool on, const float* v, size_t stride,
                                             uint32_t lane) {
-  const uint32_t am = __ballot_sync(0xffffffffu, act);
+  const uint32_t am = __ballot_sync(0xffffffffu, on);
   if (!am) return;
-  const uint32_t key = act ? (uint32_t)e : 0xffffffffu - lane;
-  const uint32_t peers = __match_any_sync(0xffffffffu, key);
-  const bool lead = act && (peers & ((1u << lane) - 1)) == 0;
-  const int nlead = __popc(__ballot_sync(0xffffffffu, lead));
   auto atomic_vec = [&](float* p, const float* x) {
     if constexpr (F == 2) {
       atomicAdd(reinterpret_cast<float2*>(p), make_float2(x[0], x[1]));
@@ -196,61 +193,60 @@ __device__ __forceinline__ void scatter_add(float* __restrict__ dst_base, int e,
       for (int f = 0; f < F; f++) atomicAdd(p + f, x[f]);
     }
   };
-  if (nlead * 4 <= __popc(am)) {
-    uint32_t rem = am;
-    while (rem) {
-      const int l0 = __ffs(rem) - 1;
-      const uint32_t k0 = __shfl_sync(0xffffffffu, key, l0);
-      const bool in = act && key == k0;
-      float x[F];
+  const int first = __ffs(am) - 1;
+  const int e0 = __shfl_sync(0xffffffffu, e, first);
+  if (__all_sync(0xffffffffu, !on || e == e0) && __popc(am) > 1) {
+    float x[F];
 #pragma unroll
-      for (int f = 0; f < F; f++) {
-        float y = in ? v[f] : 0.0f;
+    for (int f = 0; f < F; f++) {
+      float y = on ? v[f] : 0.0f;
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) y += __shfl_xor_sync(0xffffffffu, y, off);
-        x[f] = y;
-      }
-      if ((int)lane == l0) atomic_vec(dst_base + (size_t)k0 * stride, x);
-      rem &= ~__ballot_sync(0xffffffffu, in);
+      for (int off = 16; off > 0; off >>= 1) y += __shfl_xor_sync(0xffffffffu, y, off);
+      x[f] = y;
     }
-  } else if (act) {
+    if ((int)lane == first) atomic_vec(dst_base + (size_t)e0 * stride, x);
+  } else if (on) {
     atomic_vec(dst_base + (size_t)e * stride, v);
   }
 }
 
-constexpr int kBwdWarps = 4;
+constexpr int kBwdWarps = 8;
 
+// One warp per primitive, lane g = grid point g.  With dIn_p = W^T dpre_p
+// (backward.cu:608-619), every per-pair sum collapses onto O-wide vectors:
+//   v_g  = sum_p g'_{p,g} dpre_p                 -> dconf_g = v_g . (W phi_g)
+//   vA_g = sum_p [|g' conf_g| > 1e-9] g' dpre_p  -> table coefficient conf_g W^T vA_g
+//   E_g  = w_g dpre_{p(g)}                       -> dW += E_g (x) phi_g
+// so each contributing pixel costs O multiply-adds per lane, and the hashgrid
+// gather (for phi_g) and scatter (for the table gradient) share one level loop.
 template <int F, int OMAX>
-__global__ void __launch_bounds__(kBwdWarps * 32) backward_prim_kernel(Scene sc, GeomState g, float* __restrict__ dconf,
+__global__ void __launch_bounds__(kBwdWarps * 32, 3) backward_prim_kernel(Scene sc, GeomState g, float* __restrict__ dconf,
                                                                       float* __restrict__ dtable, float* __restrict__ dW,
                                                                       float* __restrict__ db) {
   extern __shared__ float smem[];
   const int L = sc.L, D = L * F, O = sc.O, V = sc.V, G = sc.G;
   const int DS = D + 1;
-  float* W_s = smem;                 // [O][D]
-  float* dW_s = W_s + OMAX * D;      // [OMAX][D]
-  float* db_s = dW_s + OMAX * D;     // [OMAX]
+  float* W_s = smem;              // [D][OMAX]: W transposed
+  float* dW_s = W_s + D * OMAX;   // [OMAX][D]
+  float* db_s = dW_s + OMAX * D;  // [OMAX]
   const int w = threadIdx.x >> 5;
   const uint32_t lane = threadIdx.x & 31;
-  float* phi_s = db_s + OMAX + w * (2 * 32 * DS + 32 * OMAX + 64);
-  float* A_s = phi_s + 32 * DS;
-  float* E_s = A_s + 32 * DS;
-  float* dIn_s = E_s + 32 * OMAX;  // [64]
+  float* phi_s = db_s + OMAX + w * (32 * DS + 32 * OMAX + OMAX * D);  // [32][DS]
+  float* E_s = phi_s + 32 * DS;                                        // [32][OMAX]
+  float* dWw = E_s + 32 * OMAX;  // [OMAX][D] this warp's dW partial sums; lane j owns columns j, j+32
+  for (int i = (int)lane; i < OMAX * D; i += 32) dWw[i] = 0.0f;
 
-  for (int i = threadIdx.x; i < OMAX * D; i += blockDim.x) {
-    W_s[i] = i < O * D ? sc.Wl[i] : 0.0f;
+  for (int i = threadIdx.x; i < D * OMAX; i += blockDim.x) {
+    const int d = i / OMAX, o = i % OMAX;
+    W_s[i] = o < O ? sc.Wl[o * D + d] : 0.0f;
     dW_s[i] = 0.0f;
   }
   for (int i = threadIdx.x; i < OMAX; i += blockDim.x) db_s[i] = 0.0f;
   __syncthreads();
 
   const Stencil st = make_stencil(sc.genus);
-  const uint32_t p0 = (uint32_t)sc.primes[0], p1 = (uint32_t)sc.primes[1], p2 = (uint32_t)sc.primes[2];
-  float dWacc[2][OMAX];
-#pragma unroll
-  for (int h = 0; h < 2; h++)
-#pragma unroll
-    for (int o = 0; o < OMAX; o++) dWacc[h][o] = 0.0f;
+  const uint32_t p0 = (uint32_t)__ldg(sc.primes), p1 = (uint32_t)__ldg(sc.primes + 1),
+                 p2 = (uint32_t)__ldg(sc.primes + 2);
   float dbacc = 0.0f;
 
   const int nwarps = gridDim.x * kBwdWarps;
@@ -272,33 +268,10 @@ __global__ void __launch_bounds__(kBwdWarps * 32) backward_prim_kernel(Scene sc,
     const float mag = act ? occ_mag(posm, lane, G, st) : 0.0f;
     const float wE = (act && conf > 0.0f && mag > 1e-7f) ? fmul(conf, mag) : 0.0f;
 
-    // Which lanes matter: own pixel contributing, or a stencil neighbour in one.
-    bool involved = false;
-    {
-      uint32_t m = cm;
-      while (m) {
-        const int j = __ffs(m) - 1;
-        m &= m - 1;
-        const uint32_t key = g.rec_key[s0 + j];
-        const uint32_t t = key >> 8;
-        const int ppx = (int)((t % sc.gx) * 16 + (key & 15u)), ppy = (int)((t / sc.gx) * 16 + ((key >> 4) & 15u));
-        const uint32_t inm = __ballot_sync(0xffffffffu, bpix == ppy * sc.W + ppx);
-        if (act && occ_mag(inm, lane, G, st) > 0.0f) involved = true;
-        if ((inm >> lane) & 1u) involved = true;
-      }
-    }
-    float* phi = phi_s + lane * DS;
-    float* A = A_s + lane * DS;
-    if (involved) {
-      gather_features<F>(sc, pos, phi);
-      for (int i = 0; i < D; i++) A[i] = 0.0f;
-    }
+    float v[OMAX], vA[OMAX];
 #pragma unroll
-    for (int o = 0; o < OMAX; o++) E_s[lane * OMAX + o] = 0.0f;
-    float dX = 0.0f;
-    bool hasA = false;
-    __syncwarp();
-
+    for (int o = 0; o < OMAX; o++) v[o] = vA[o] = 0.0f;
+    bool hasE = false, hasV = false, hasA = false;
     uint32_t m = cm;
     while (m) {
       const int j = __ffs(m) - 1;
@@ -311,106 +284,121 @@ __global__ void __launch_bounds__(kBwdWarps * 32) backward_prim_kernel(Scene sc,
       const float4* src = reinterpret_cast<const float4*>(g.rec_dpre + slot * OMAX);
 #pragma unroll
       for (int o4 = 0; o4 < OMAX / 4; o4++) {
-        float4 v = src[o4];
-        dpre[4 * o4] = v.x; dpre[4 * o4 + 1] = v.y; dpre[4 * o4 + 2] = v.z; dpre[4 * o4 + 3] = v.w;
+        const float4 x = src[o4];
+        dpre[4 * o4] = x.x; dpre[4 * o4 + 1] = x.y; dpre[4 * o4 + 2] = x.z; dpre[4 * o4 + 3] = x.w;
       }
 #pragma unroll
       for (int o = 0; o < OMAX; o++)
         if ((int)lane == o) dbacc += dpre[o];
       const uint32_t inm = __ballot_sync(0xffffffffu, bpix == ppy * sc.W + ppx);
       if (((inm >> lane) & 1u) && wE != 0.0f) {
+        hasE = true;
 #pragma unroll
         for (int o = 0; o < OMAX; o++) E_s[lane * OMAX + o] = fmul(wE, dpre[o]);
       }
-      for (int jj = lane; jj < D; jj += 32) {
-        float s = 0.0f;
-#pragma unroll
-        for (int o = 0; o < OMAX; o++) s += dpre[o] * W_s[o * D + jj];
-        dIn_s[jj] = s;
-      }
-      __syncwarp();
       const float gp = act ? occ_mag(inm, lane, G, st) : 0.0f;
       if (gp > 1e-7f) {
-        const float wp = fmul(gp, conf);
-        const bool doA = fabsf(wp) > 1e-9f;
-        float sdot = 0.0f;
-        if (doA) {
-          hasA = true;
-          for (int i = 0; i < D; i++) {
-            const float d = dIn_s[i];
-            sdot += d * phi[i];
-            A[i] += d * wp;
-          }
-        } else {
-          for (int i = 0; i < D; i++) sdot += dIn_s[i] * phi[i];
-        }
-        dX += sdot * gp;
-      }
-      __syncwarp();
-    }
-    if (act) dconf[s0 + lane] = dX;
-
-    // dW += E_g (x) phi_g over grid points with an E contribution.
-    const uint32_t em = __ballot_sync(0xffffffffu, ((int)lane < V) && involved && wE != 0.0f);
-    __syncwarp();
+        hasV = true;
+        const bool doA = fabsf(fmul(gp, conf)) > 1e-9f;
+        hasA |= doA;
 #pragma unroll
-    for (int h = 0; h < 2; h++) {
-      const int jj = (int)lane + 32 * h;
-      if (jj < D) {
-        uint32_t mm = em;
-        while (mm) {
-          const int gg = __ffs(mm) - 1;
-          mm &= mm - 1;
-          const float x = phi_s[gg * DS + jj];
-#pragma unroll
-          for (int o = 0; o < OMAX; o++) dWacc[h][o] += E_s[gg * OMAX + o] * x;
+        for (int o = 0; o < OMAX; o++) {
+          const float x = gp * dpre[o];
+          v[o] += x;
+          if (doA) vA[o] += x;
         }
       }
     }
+    if (!__any_sync(0xffffffffu, hasE || hasV)) continue;
 
-    // Hash-table scatter of A (dz, dy, dx corner order as hashgrid.h:43-45).
-    if (__any_sync(0xffffffffu, hasA)) {
-      for (int l = 0; l < L; l++) {
-        const int res = __ldg(sc.res + l);
-        const bool hsh = __ldg(sc.do_hash + l) != 0;
-        int3 b;
-        float3 tt;
-        level_setup(pos, res, b, tt);
-        float a[F];
+    // One pass over the levels: gather phi_g (for dconf and dW), scatter the table gradient.
+    float mlp[OMAX];
 #pragma unroll
-        for (int f = 0; f < F; f++) a[f] = hasA ? A[l * F + f] : 0.0f;
+    for (int o = 0; o < OMAX; o++) mlp[o] = 0.0f;
+    float* phi_row = phi_s + lane * DS;
+    const bool gather = hasE || hasV;
+    const float3 nrm = hash_norm(pos);
+#pragma unroll 1
+    for (int l = 0; l < L; l++) {
+      const int res = __ldg(sc.res + l);
+      const bool hsh = __ldg(sc.do_hash + l) != 0;
+      int3 b;
+      float3 tt;
+      level_setup_n(nrm, res, b, tt);
+      float acc[F], a[F];
 #pragma unroll
-        for (int dz = 0; dz < 2; dz++)
+      for (int f = 0; f < F; f++) {
+        acc[f] = 0.0f;
+        // table coefficient of this level: conf_g * sum_o W[o][l*F+f] vA[o]
+        float s = 0.0f;
+        const float* wr = W_s + (l * F + f) * OMAX;
 #pragma unroll
-          for (int dy = 0; dy < 2; dy++)
+        for (int o = 0; o < OMAX; o++) s += wr[o] * vA[o];
+        a[f] = conf * s;
+      }
+      const float* lvl = sc.table + (size_t)l * F;
 #pragma unroll
-            for (int dx = 0; dx < 2; dx++) {
-              float cw = 1.0f;
-              cw *= dx == 1 ? tt.x : 1.0f - tt.x;
-              cw *= dy == 1 ? tt.y : 1.0f - tt.y;
-              cw *= dz == 1 ? tt.z : 1.0f - tt.z;
-              const int e = corner_entry(b.x + dx, b.y + dy, b.z + dz, res, hsh, p0, p1, p2, sc.T, sc.Tmask);
-              const bool on = hasA && e >= 0 && cw != 0.0f;
-              float v[F];
+      for (int dz = 0; dz < 2; dz++)
 #pragma unroll
-              for (int f = 0; f < F; f++) v[f] = a[f] * cw;
-              scatter_add<F>(dtable + (size_t)l * F, e, on, v, (size_t)L * F, lane);
+        for (int dy = 0; dy < 2; dy++)
+#pragma unroll
+          for (int dx = 0; dx < 2; dx++) {
+            const float wx = dx == 1 ? tt.x : 1.0f - tt.x;
+            const float wy = dy == 1 ? tt.y : 1.0f - tt.y;
+            const float wz = dz == 1 ? tt.z : 1.0f - tt.z;
+            const float cw = wx * wy * wz;
+            const int e = (cw != 0.0f) ? corner_entry(b.x + dx, b.y + dy, b.z + dz, res, hsh, p0, p1, p2, sc.T, sc.Tmask)
+                                       : -1;
+            if (gather && e >= 0) {
+              const FVec<F> x = load_feat<F>(lvl + (size_t)e * L * F);
+#pragma unroll
+              for (int f = 0; f < F; f++) acc[f] += x.v[f] * cw;
             }
+            float val[F];
+#pragma unroll
+            for (int f = 0; f < F; f++) val[f] = a[f] * cw;
+            scatter_add<F>(dtable + (size_t)l * F, e, hasA && e >= 0, val, (size_t)L * F, lane);
+          }
+#pragma unroll
+      for (int f = 0; f < F; f++) {
+        const float x = acc[f];
+        const float* wr = W_s + (l * F + f) * OMAX;
+#pragma unroll
+        for (int o = 0; o < OMAX; o++) mlp[o] += wr[o] * x;
+        if (hasE) phi_row[l * F + f] = x;
       }
+    }
+    if (act) {
+      float dX = 0.0f;
+#pragma unroll
+      for (int o = 0; o < OMAX; o++) dX += v[o] * mlp[o];
+      dconf[s0 + lane] = dX;
+    }
+    // dW += E_g (x) phi_g over the lanes with an E contribution.
+    const uint32_t em = __ballot_sync(0xffffffffu, hasE);
+    __syncwarp();
+    for (int jj = (int)lane; jj < D; jj += 32) {
+      float acc[OMAX];
+#pragma unroll
+      for (int o = 0; o < OMAX; o++) acc[o] = dWw[o * D + jj];
+      uint32_t mm = em;
+      while (mm) {
+        const int gg = __ffs(mm) - 1;
+        mm &= mm - 1;
+        const float x = phi_s[gg * DS + jj];
+#pragma unroll
+        for (int o = 0; o < OMAX; o++) acc[o] += E_s[gg * OMAX + o] * x;
+      }
+#pragma unroll
+      for (int o = 0; o < OMAX; o++) dWw[o * D + jj] = acc[o];
     }
     __syncwarp();
   }
 
   // CTA reduction of dW and db, then one global atomic per element.
-#pragma unroll
-  for (int h = 0; h < 2; h++) {
-    const int jj = (int)lane + 32 * h;
-    if (jj < D) {
-#pragma unroll
-      for (int o = 0; o < OMAX; o++)
-        if (o < O && dWacc[h][o] != 0.0f) atomicAdd(&dW_s[o * D + jj], dWacc[h][o]);
-    }
-  }
+  __syncwarp();
+  for (int i = (int)lane; i < O * D; i += 32)
+    if (dWw[i] != 0.0f) atomicAdd(&dW_s[i], dWw[i]);
   if ((int)lane < O && dbacc != 0.0f) atomicAdd(&db_s[lane], dbacc);
   __syncthreads();
   for (int i = threadIdx.x; i < O * D; i += blockDim.x)
@@ -422,13 +410,14 @@ __global__ void __launch_bounds__(kBwdWarps * 32) backward_prim_kernel(Scene sc,
 template <int F, int OMAX>
 void launch_prim_t(const Scene& sc, GeomState& g, float* dconf, float* dtable, float* dW, float* db, cudaStream_t s) {
   const int D = sc.L * F;
-  size_t smem = sizeof(float) * (2 * OMAX * D + OMAX + kBwdWarps * (2 * 32 * (D + 1) + 32 * OMAX + 64));
+  size_t smem = sizeof(float) * (2 * OMAX * D + OMAX + kBwdWarps * (32 * (D + 1) + 32 * OMAX + OMAX * D));
   auto k = backward_prim_kernel<F, OMAX>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   int blocks = (sc.P + kBwdWarps - 1) / kBwdWarps;
-  blocks = blocks < 148 * 16 ? blocks : 148 * 16;
+  blocks = blocks < 148 * 8 ? blocks : 148 * 8;
   if (blocks < 1) blocks = 1;
   k<<<blocks, kBwdWarps * 32, smem, s>>>(sc, g, dconf, dtable, dW, db);
+  note_launches(1);
 }
 
 }  // namespace
@@ -438,13 +427,17 @@ void launch_backward(const Scene& sc, GeomState& g, const ImgState& im, const fl
   const size_t N = (size_t)sc.W * sc.H;
   cudaMemsetAsync(g.rec_flag, 0, (size_t)sc.P * sc.V, s);
   const bool o16 = sc.O > 8;
+  stage_begin(kStBwdPixel, s);
   if (N > 0) {
+    note_launches(1);
     const unsigned blocks = (unsigned)((N + 255) / 256);
     if (o16)
       backward_pixel_kernel<16><<<blocks, 256, 0, s>>>(sc, g, im, dL_dcolor, dL_dfeat);
     else
       backward_pixel_kernel<8><<<blocks, 256, 0, s>>>(sc, g, im, dL_dcolor, dL_dfeat);
   }
+  stage_end(kStBwdPixel, s);
+  stage_begin(kStBwdPrim, s);
   switch (sc.F) {
     case 1: o16 ? launch_prim_t<1, 16>(sc, g, dconf, dtable, dW, db, s) : launch_prim_t<1, 8>(sc, g, dconf, dtable, dW, db, s); break;
     case 2: o16 ? launch_prim_t<2, 16>(sc, g, dconf, dtable, dW, db, s) : launch_prim_t<2, 8>(sc, g, dconf, dtable, dW, db, s); break;
@@ -452,6 +445,7 @@ void launch_backward(const Scene& sc, GeomState& g, const ImgState& im, const fl
     case 8: o16 ? launch_prim_t<8, 16>(sc, g, dconf, dtable, dW, db, s) : launch_prim_t<8, 8>(sc, g, dconf, dtable, dW, db, s); break;
     default: break;
   }
+  stage_end(kStBwdPrim, s);
 }
 
 }  // namespace vi

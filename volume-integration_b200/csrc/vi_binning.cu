@@ -205,6 +205,7 @@ __global__ void __launch_bounds__(256) mark_visible_kernel(int P, const float* _
 void launch_preprocess(const Scene& sc, GeomState& g, cudaStream_t s) {
   if (sc.P == 0) return;
   preprocess_kernel<<<(sc.P + 255) / 256, 256, 0, s>>>(sc, g);
+  note_launches(1);
 }
 
 void launch_offsets_scan(const Scene& sc, GeomState& g, const uint32_t* sorted_idx, cudaStream_t s) {
@@ -212,22 +213,26 @@ void launch_offsets_scan(const Scene& sc, GeomState& g, const uint32_t* sorted_i
   scan_reduce_kernel<<<nb, 256, 0, s>>>(sc.P, sorted_idx, g.tiles_touched, g.block_sums);
   scan_blocks_kernel<<<1, 1024, 0, s>>>(nb, g.block_sums, g.status);
   scan_down_kernel<<<nb, 256, 0, s>>>(sc.P, sorted_idx, g.tiles_touched, g.block_sums, g.offsets);
+  note_launches(3);
 }
 
 void launch_duplicate(const Scene& sc, const GeomState& g, const uint32_t* sorted_idx, BinState& b, cudaStream_t s) {
   duplicate_kernel<<<(sc.P + 255) / 256, 256, 0, s>>>(sc, g.radii, g.means2D, g.tiles_touched, sorted_idx, g.offsets,
                                                       b.tkeys, b.tvals);
+  note_launches(1);
 }
 
 void launch_ranges(uint64_t R, const uint32_t* sorted_tiles, uint32_t* ranges, size_t tiles, cudaStream_t s) {
   cudaMemsetAsync(ranges, 0, tiles * 2 * sizeof(uint32_t), s);
   if (R == 0) return;
   ranges_kernel<<<(unsigned)((R + 255) / 256), 256, 0, s>>>(R, sorted_tiles, ranges);
+  note_launches(1);
 }
 
 void launch_mark_visible(int P, const float* means, const float* view, bool* present, cudaStream_t s) {
   if (P == 0) return;
   mark_visible_kernel<<<(P + 255) / 256, 256, 0, s>>>(P, means, view, present);
+  note_launches(1);
 }
 
 

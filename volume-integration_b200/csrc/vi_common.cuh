@@ -79,13 +79,28 @@ __device__ __forceinline__ float3 grid_pos(float3 c, int g, int G, float step, f
   return p;
 }
 
-// Hashgrid level set-up (hashgrid.h:225-242): integer base corner and fractions.
-__device__ __forceinline__ void level_setup(float3 pos, int res, int3& b, float3& t) {
-  float nx = fmaxf(0.0f, fminf(1.0f, __fdiv_rn(fsub(pos.x, -1.3f), 2.6f)));
-  float ny = fmaxf(0.0f, fminf(1.0f, __fdiv_rn(fsub(pos.y, -1.3f), 2.6f)));
-  float nz = fmaxf(0.0f, fminf(1.0f, __fdiv_rn(fsub(pos.z, -1.3f), 2.6f)));
+// Position normalised to the fixed scene box [-1.3, 1.3]^3 and clamped to [0, 1]
+// (hashgrid.h:225-235).  It does not depend on the level, so callers compute it
+// once per point.
+__device__ __forceinline__ float3 hash_norm(float3 pos) {
+  return make_float3(fmaxf(0.0f, fminf(1.0f, __fdiv_rn(fsub(pos.x, -1.3f), 2.6f))),
+                     fmaxf(0.0f, fminf(1.0f, __fdiv_rn(fsub(pos.y, -1.3f), 2.6f))),
+                     fmaxf(0.0f, fminf(1.0f, __fdiv_rn(fsub(pos.z, -1.3f), 2.6f))));
+}
+
+// Hashgrid level set-up (hashgrid.h:237-242): integer base corner and fractions.
+__device__ __forceinline__ void level_setup_n(float3 n, int res, int3& b, float3& t) {
   float rf = (float)res;
-  float px = fmul(nx, rf), py = fmul(ny, rf), pz = fmul(nz, rf);
+  float px = fmul(n.x, rf), py = fmul(n.y, rf), pz = fmul(n.z, rf);
+  float fx = floorf(px), fy = floorf(py), fz = floorf(pz);
+  b = make_int3((int)fx, (int)fy, (int)fz);
+  t = make_float3(fsub(px, fx), fsub(py, fy), fsub(pz, fz));
+}
+
+__device__ __forceinline__ void level_setup(float3 pos, int res, int3& b, float3& t) {
+  float3 n = hash_norm(pos);
+  float rf = (float)res;
+  float px = fmul(n.x, rf), py = fmul(n.y, rf), pz = fmul(n.z, rf);
   float fx = floorf(px), fy = floorf(py), fz = floorf(pz);
   b = make_int3((int)fx, (int)fy, (int)fz);
   t = make_float3(fsub(px, fx), fsub(py, fy), fsub(pz, fz));

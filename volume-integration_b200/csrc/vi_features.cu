@@ -27,13 +27,11 @@ template <int F, int OMAX>
 __global__ void __launch_bounds__(kFeatWarps * 32) features_kernel(Scene sc, GeomState g) {
   extern __shared__ float smem[];
   const int D = sc.L * F, O = sc.O, V = sc.V, G = sc.G;
-  const int DS = D + 1;  // padded row stride of phi
   float* W_s = smem;                       // [D][OMAX] (transposed for broadcast reads)
   float* b_s = W_s + D * OMAX;             // [OMAX]
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* phi_s = b_s + OMAX + w * (32 * DS + 32 * OMAX + 32);  // [32][DS]
-  float* c_s = phi_s + 32 * DS;                                 // [32][OMAX]
-  float* mag_s = c_s + 32 * OMAX;                               // [32]
+  float* c_s = b_s + OMAX + w * (32 * OMAX + 32);  // [32][OMAX]
+  float* mag_s = c_s + 32 * OMAX;                   // [32]
 
   for (int i = threadIdx.x; i < D * OMAX; i += blockDim.x) {
     int d = i / OMAX, o = i % OMAX;
@@ -79,23 +77,25 @@ __global__ void __launch_bounds__(kFeatWarps * 32) features_kernel(Scene sc, Geo
 #pragma unroll
     for (int o = 0; o < OMAX; o++) cvec[o] = 0.0f;
     if (need) {
-      float* phi = phi_s + lane * DS;
-      gather_features<F>(sc, pos, phi);
+      // Linear layer accumulated level by level: mlp[o] = sum_i W[o][i] phi[i], i ascending.
       float mlp[OMAX];
 #pragma unroll
       for (int o = 0; o < OMAX; o++) mlp[o] = 0.0f;
-      for (int i = 0; i < D; i++) {
-        const float x = phi[i];
-        const float4* wr = reinterpret_cast<const float4*>(W_s + i * OMAX);
+      for_each_level<F>(sc, pos, [&](int l, const float* phi, int3, float3, int, bool) {
 #pragma unroll
-        for (int o4 = 0; o4 < OMAX / 4; o4++) {
-          float4 ww = wr[o4];
-          mlp[4 * o4 + 0] += ww.x * x;
-          mlp[4 * o4 + 1] += ww.y * x;
-          mlp[4 * o4 + 2] += ww.z * x;
-          mlp[4 * o4 + 3] += ww.w * x;
+        for (int f = 0; f < F; f++) {
+          const float x = phi[f];
+          const float4* wr = reinterpret_cast<const float4*>(W_s + (l * F + f) * OMAX);
+#pragma unroll
+          for (int o4 = 0; o4 < OMAX / 4; o4++) {
+            const float4 ww = wr[o4];
+            mlp[4 * o4 + 0] += ww.x * x;
+            mlp[4 * o4 + 1] += ww.y * x;
+            mlp[4 * o4 + 2] += ww.z * x;
+            mlp[4 * o4 + 3] += ww.w * x;
+          }
         }
-      }
+      });
       const float wgt = fmul(conf, mag);
 #pragma unroll
       for (int o = 0; o < OMAX; o++) cvec[o] = fmul(mlp[o], wgt);
@@ -157,13 +157,14 @@ __global__ void __launch_bounds__(kFeatWarps * 32) features_kernel(Scene sc, Geo
 template <int F, int OMAX>
 void launch_features_t(const Scene& sc, GeomState& g, cudaStream_t s) {
   const int D = sc.L * F;
-  size_t smem = sizeof(float) * (D * OMAX + OMAX + kFeatWarps * (32 * (D + 1) + 32 * OMAX + 32));
+  size_t smem = sizeof(float) * (D * OMAX + OMAX + kFeatWarps * (32 * OMAX + 32));
   auto k = features_kernel<F, OMAX>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   int blocks = (sc.P + kFeatWarps - 1) / kFeatWarps;
   blocks = blocks < 148 * 16 ? blocks : 148 * 16;
   if (blocks < 1) blocks = 1;
   k<<<blocks, kFeatWarps * 32, smem, s>>>(sc, g);
+  note_launches(1);
 }
 
 }  // namespace

@@ -12,6 +12,15 @@ constexpr int kRadix = 256;
 
 inline size_t align_up(size_t x, size_t a = 256) { return (x + a - 1) / a * a; }
 
+// Number of kernels this library has launched (all threads), for launch accounting.
+void note_launches(int n);
+
+// Optional per-stage CUDA-event timing on the launching stream.
+enum Stage { kStPreprocess, kStDepthSort, kStOffsets, kStFeatures, kStBinning, kStRender, kStBwdPixel, kStBwdPrim,
+             kStCount };
+void stage_begin(Stage st, cudaStream_t s);
+void stage_end(Stage st, cudaStream_t s);
+
 // Scratch of one onesweep sort (see vi_sort.cu).
 struct SortTemp {
   uint32_t* hist = nullptr;      // passes x 256 digit counts, then exclusive starts

@@ -67,42 +67,50 @@ __device__ __forceinline__ FVec<F> load_feat(const float* __restrict__ p) {
   return r;
 }
 
-// Trilinear hashgrid features of one point at every level (hashgrid.h:207-299),
-// written to phi[l*F + f].  Corners visited dx, dy, dz as the reference does.
-template <int F>
-__device__ __forceinline__ void gather_features(const Scene& sc, float3 pos, float* phi) {
-  const uint32_t p0 = (uint32_t)sc.primes[0], p1 = (uint32_t)sc.primes[1], p2 = (uint32_t)sc.primes[2];
+// Trilinear hashgrid features of one point, level by level (hashgrid.h:207-299).
+// For each level, fn(l, acc) receives the F interpolated features.  Corners
+// are visited dx, dy, dz as the reference does; corners whose trilinear weight
+// is exactly zero are skipped (their product with a finite table value is
+// zero, so the sum is unchanged), which is most corners of points clamped to
+// the faces of the hashgrid box.
+template <int F, typename Fn>
+__device__ __forceinline__ void for_each_level(const Scene& sc, float3 pos, Fn&& fn) {
+  const uint32_t p0 = (uint32_t)__ldg(sc.primes), p1 = (uint32_t)__ldg(sc.primes + 1),
+                 p2 = (uint32_t)__ldg(sc.primes + 2);
+  const float3 nrm = hash_norm(pos);
+#pragma unroll 2
   for (int l = 0; l < sc.L; l++) {
     const int res = __ldg(sc.res + l);
     const bool hsh = __ldg(sc.do_hash + l) != 0;
     int3 b;
     float3 t;
-    level_setup(pos, res, b, t);
+    level_setup_n(nrm, res, b, t);
     float acc[F];
 #pragma unroll
     for (int f = 0; f < F; f++) acc[f] = 0.0f;
     const float* lvl = sc.table + (size_t)l * F;
 #pragma unroll
     for (int dx = 0; dx < 2; dx++) {
-      float wx = dx == 0 ? 1.0f - t.x : t.x;
+      const float wx = dx == 0 ? 1.0f - t.x : t.x;
 #pragma unroll
       for (int dy = 0; dy < 2; dy++) {
-        float wy = dy == 0 ? 1.0f - t.y : t.y;
+        const float wy = dy == 0 ? 1.0f - t.y : t.y;
 #pragma unroll
         for (int dz = 0; dz < 2; dz++) {
-          float wz = dz == 0 ? 1.0f - t.z : t.z;
-          float w = wx * wy * wz;
-          int e = corner_entry(b.x + dx, b.y + dy, b.z + dz, res, hsh, p0, p1, p2, sc.T, sc.Tmask);
-          if (e >= 0) {
-            FVec<F> v = load_feat<F>(lvl + (size_t)e * sc.L * F);
+          const float wz = dz == 0 ? 1.0f - t.z : t.z;
+          const float w = wx * wy * wz;
+          if (w != 0.0f) {
+            const int e = corner_entry(b.x + dx, b.y + dy, b.z + dz, res, hsh, p0, p1, p2, sc.T, sc.Tmask);
+            if (e >= 0) {
+              const FVec<F> v = load_feat<F>(lvl + (size_t)e * sc.L * F);
 #pragma unroll
-            for (int f = 0; f < F; f++) acc[f] += v.v[f] * w;
+              for (int f = 0; f < F; f++) acc[f] += v.v[f] * w;
+            }
           }
         }
       }
     }
-#pragma unroll
-    for (int f = 0; f < F; f++) phi[l * F + f] = acc[f];
+    fn(l, acc, b, t, res, hsh);
   }
 }
 

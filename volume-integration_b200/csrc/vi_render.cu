@@ -160,6 +160,7 @@ void launch_render(const Scene& sc, const GeomState& g, const uint32_t* point_li
                    float* out_feat, float* vis, cudaStream_t s) {
   const unsigned tiles = sc.gx * sc.gy;
   if (tiles == 0) return;
+  note_launches(1);
   if (sc.O > 8)
     render_kernel<16><<<tiles, VI_TILE_PIX, 0, s>>>(sc, point_list, im.ranges, g.depths, g.rec_cnt, g.rec_key,
                                                     g.rec_props, out_color, out_feat, vis, im.final_T, im.n_contrib,

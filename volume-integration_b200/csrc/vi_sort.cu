@@ -229,6 +229,7 @@ bool sort_impl(K* keys, uint32_t* vals, K* alt_keys, uint32_t* alt_vals, uint64_
   cudaMemsetAsync(t.lookback, 0, sizeof(uint32_t) * kRadix * (size_t)t.tiles * passes, s);
   int hblocks = (int)std::min<uint64_t>((n + 255) / 256, 148 * 8);
   hist_kernel<K><<<hblocks, 256, 0, s>>>(keys, n, begin_bit, end_bit, passes, t.hist);
+  note_launches(2 + passes);
   hist_scan_kernel<<<passes, kRadix, 0, s>>>(t.hist);
   K* kin = keys;
   uint32_t* vin = vals;
