@@ -249,8 +249,18 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) backward_prim_kernel(Scene 
                  p2 = (uint32_t)__ldg(sc.primes + 2);
   float dbacc = 0.0f;
 
-  const int nwarps = gridDim.x * kBwdWarps;
-  for (int q = blockIdx.x * kBwdWarps + w; q < sc.P; q += nwarps) {
+  // Primitives are handed out in batches of kGrab per warp from a counter
+  // (status[5]): warps that draw cheap primitives take more, so no warp idles at
+  // the final reduction while the counter sees one atomic per batch.
+  constexpr int kGrab = 8;
+  for (int q0 = 0, qi = kGrab;;) {
+    if (qi == kGrab) {
+      if (lane == 0) q0 = (int)atomicAdd(g.status + 5, (unsigned)kGrab);
+      q0 = __shfl_sync(0xffffffffu, q0, 0);
+      qi = 0;
+    }
+    const int q = q0 + qi++;
+    if (q >= sc.P) break;
     const uint32_t n = g.rec_cnt[q] & ~kBwdDiffers;
     if (n == 0) continue;
     const size_t s0 = (size_t)q * V;
@@ -330,35 +340,38 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) backward_prim_kernel(Scene 
       for (int f = 0; f < F; f++) {
         acc[f] = 0.0f;
         // table coefficient of this level: conf_g * sum_o W[o][l*F+f] vA[o]
-        float s = 0.0f;
+        float sum = 0.0f;
         const float* wr = W_s + (l * F + f) * OMAX;
 #pragma unroll
-        for (int o = 0; o < OMAX; o++) s += wr[o] * vA[o];
-        a[f] = conf * s;
+        for (int o = 0; o < OMAX; o++) sum += wr[o] * vA[o];
+        a[f] = conf * sum;
       }
+      // Corners with a nonzero trilinear weight: an axis whose fraction is 0
+      // contributes only its lower corner.  Bit (dx + 2 dy + 4 dz).
+      const uint32_t mx = tt.x != 0.0f ? 0xffu : 0x55u, my = tt.y != 0.0f ? 0xffu : 0x33u,
+                     mz = tt.z != 0.0f ? 0xffu : 0x0fu;
+      const uint32_t cmask = (gather || hasA) ? (mx & my & mz) : 0u;
+      const int kmax = (int)__reduce_max_sync(0xffffffffu, (unsigned)__popc(cmask));
       const float* lvl = sc.table + (size_t)l * F;
+      for (int k = 0; k < kmax; k++) {
+        int e = -1;
+        float cw = 0.0f;
+        if (k < __popc(cmask)) {
+          const int cidx = __fns(cmask, 0, k + 1);
+          const int dx = cidx & 1, dy = (cidx >> 1) & 1, dz = cidx >> 2;
+          cw = (dx ? tt.x : 1.0f - tt.x) * (dy ? tt.y : 1.0f - tt.y) * (dz ? tt.z : 1.0f - tt.z);
+          e = cw != 0.0f ? corner_entry(b.x + dx, b.y + dy, b.z + dz, res, hsh, p0, p1, p2, sc.T, sc.Tmask) : -1;
+        }
+        if (gather && e >= 0) {
+          const FVec<F> x = load_feat<F>(lvl + (size_t)e * L * F);
 #pragma unroll
-      for (int dz = 0; dz < 2; dz++)
+          for (int f = 0; f < F; f++) acc[f] += x.v[f] * cw;
+        }
+        float val[F];
 #pragma unroll
-        for (int dy = 0; dy < 2; dy++)
-#pragma unroll
-          for (int dx = 0; dx < 2; dx++) {
-            const float wx = dx == 1 ? tt.x : 1.0f - tt.x;
-            const float wy = dy == 1 ? tt.y : 1.0f - tt.y;
-            const float wz = dz == 1 ? tt.z : 1.0f - tt.z;
-            const float cw = wx * wy * wz;
-            const int e = (cw != 0.0f) ? corner_entry(b.x + dx, b.y + dy, b.z + dz, res, hsh, p0, p1, p2, sc.T, sc.Tmask)
-                                       : -1;
-            if (gather && e >= 0) {
-              const FVec<F> x = load_feat<F>(lvl + (size_t)e * L * F);
-#pragma unroll
-              for (int f = 0; f < F; f++) acc[f] += x.v[f] * cw;
-            }
-            float val[F];
-#pragma unroll
-            for (int f = 0; f < F; f++) val[f] = a[f] * cw;
-            scatter_add<F>(dtable + (size_t)l * F, e, hasA && e >= 0, val, (size_t)L * F, lane);
-          }
+        for (int f = 0; f < F; f++) val[f] = a[f] * cw;
+        scatter_add<F>(dtable + (size_t)l * F, e, hasA && e >= 0, val, (size_t)L * F, lane);
+      }
 #pragma unroll
       for (int f = 0; f < F; f++) {
         const float x = acc[f];
@@ -413,6 +426,7 @@ void launch_prim_t(const Scene& sc, GeomState& g, float* dconf, float* dtable, f
   size_t smem = sizeof(float) * (2 * OMAX * D + OMAX + kBwdWarps * (32 * (D + 1) + 32 * OMAX + OMAX * D));
   auto k = backward_prim_kernel<F, OMAX>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaMemsetAsync(g.status + 5, 0, sizeof(uint32_t), s);
   int blocks = (sc.P + kBwdWarps - 1) / kBwdWarps;
   blocks = blocks < 148 * 8 ? blocks : 148 * 8;
   if (blocks < 1) blocks = 1;

@@ -161,7 +161,7 @@ void launch_features_t(const Scene& sc, GeomState& g, cudaStream_t s) {
   auto k = features_kernel<F, OMAX>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   int blocks = (sc.P + kFeatWarps - 1) / kFeatWarps;
-  blocks = blocks < 148 * 16 ? blocks : 148 * 16;
+  blocks = blocks < 148 * 8 ? blocks : 148 * 8;
   if (blocks < 1) blocks = 1;
   k<<<blocks, kFeatWarps * 32, smem, s>>>(sc, g);
   note_launches(1);

@@ -136,6 +136,10 @@ CONFIGS = {
     "headline": dict(P=1_000_000, layout="mix", clusters=256, extent=10.0, mu_scale=-5.0, mu_conf=0.0,
                      width=1920, height=1080, fov=50.0, dist=12.0, views=1, L=16, F=2, log2_T=19,
                      base=16, growth=1.447),
+    # the headline scene and camera with a quarter of the primitives (profiling case)
+    "headline_q": dict(P=250_000, layout="mix", clusters=256, extent=10.0, mu_scale=-5.0, mu_conf=0.0,
+                       width=1920, height=1080, fov=50.0, dist=12.0, views=1, L=16, F=2, log2_T=19,
+                       base=16, growth=1.447),
     "multiview": dict(P=3_000_000, layout="mix", clusters=256, extent=10.0, mu_scale=-5.0, mu_conf=0.0,
                       width=1920, height=1080, fov=50.0, dist=12.0, views=32, L=16, F=2, log2_T=19,
                       base=16, growth=1.447),
@@ -143,7 +147,7 @@ CONFIGS = {
                    width=3840, height=2160, fov=50.0, dist=14.0, views=1, L=16, F=4, log2_T=21,
                    base=16, growth=1.447),
 }
-SEEDS = {"tiny": 1000, "mid": 1001, "headline": 1002, "multiview": 1003, "stress": 1004}
+SEEDS = {"tiny": 1000, "mid": 1001, "headline": 1002, "multiview": 1003, "stress": 1004, "headline_q": 1002}
 
 
 def make(name, table_range=1e-4, seed=None, **over):
