@@ -134,7 +134,7 @@ GeomState geom_layout(char* base, size_t P, int V, int O) {
   g.rec_cnt = c.take<uint32_t>(P);
   g.rec_key = c.take<uint32_t>(P * V);
   g.rec_props = c.take<float>(P * V * OP);
-  g.rec_flag = c.take<uint8_t>(P * V);
+  g.rec_pix = c.take<uint32_t>(P * V);
   g.rec_dpre = c.take<float>(P * V * OP);
   char* st = c.take<char>(sort_temp_bytes(P, 4, 0, 32));
   sort_temp_carve(st, P, 4, 0, 32, g.sort);

@@ -159,7 +159,7 @@ __global__ void __launch_bounds__(256) backward_pixel_kernel(Scene sc, GeomState
     float4* dst = reinterpret_cast<float4*>(g.rec_dpre + (size_t)rec * OMAX);
 #pragma unroll
     for (int o4 = 0; o4 < OMAX / 4; o4++) dst[o4] = make_float4(dpre[4 * o4], dpre[4 * o4 + 1], dpre[4 * o4 + 2], dpre[4 * o4 + 3]);
-    g.rec_flag[rec] = 1;
+    g.rec_pix[rec] = (uint32_t)pix + 1u;
 #pragma unroll
     for (int d = 0; d < OMAX - 1; d++) {
       if (d < B) {
@@ -171,46 +171,26 @@ __global__ void __launch_bounds__(256) backward_pixel_kernel(Scene sc, GeomState
   }
 }
 
-// Adds v (F floats) at table slot e for every lane with `on`.  When every active
-// lane targets the same slot -- points clamped to the hashgrid box all land on one
-// corner cell -- the values are summed across the warp first and one vector
-// atomic is issued; otherwise each lane issues its own vector atomic.
 template <int F>
-__device__ __forceinline__ void scatter_add(float* __restrict__ dst_base, int e, bool on, const float* v, size_t stride,
-                                            uint32_t lane) {
-  const uint32_t am = __ballot_sync(0xffffffffu, on);
-  if (!am) return;
-  auto atomic_vec = [&](float* p, const float* x) {
-    if constexpr (F == 2) {
-      atomicAdd(reinterpret_cast<float2*>(p), make_float2(x[0], x[1]));
-    } else if constexpr (F == 4) {
-      atomicAdd(reinterpret_cast<float4*>(p), make_float4(x[0], x[1], x[2], x[3]));
-    } else if constexpr (F == 8) {
-      atomicAdd(reinterpret_cast<float4*>(p), make_float4(x[0], x[1], x[2], x[3]));
-      atomicAdd(reinterpret_cast<float4*>(p) + 1, make_float4(x[4], x[5], x[6], x[7]));
-    } else {
+__device__ __forceinline__ void atomic_vec(float* p, const float* x) {
+  if constexpr (F == 2) {
+    atomicAdd(reinterpret_cast<float2*>(p), make_float2(x[0], x[1]));
+  } else if constexpr (F == 4) {
+    atomicAdd(reinterpret_cast<float4*>(p), make_float4(x[0], x[1], x[2], x[3]));
+  } else if constexpr (F == 8) {
+    atomicAdd(reinterpret_cast<float4*>(p), make_float4(x[0], x[1], x[2], x[3]));
+    atomicAdd(reinterpret_cast<float4*>(p) + 1, make_float4(x[4], x[5], x[6], x[7]));
+  } else {
 #pragma unroll
-      for (int f = 0; f < F; f++) atomicAdd(p + f, x[f]);
-    }
-  };
-  const int first = __ffs(am) - 1;
-  const int e0 = __shfl_sync(0xffffffffu, e, first);
-  if (__all_sync(0xffffffffu, !on || e == e0) && __popc(am) > 1) {
-    float x[F];
-#pragma unroll
-    for (int f = 0; f < F; f++) {
-      float y = on ? v[f] : 0.0f;
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) y += __shfl_xor_sync(0xffffffffu, y, off);
-      x[f] = y;
-    }
-    if ((int)lane == first) atomic_vec(dst_base + (size_t)e0 * stride, x);
-  } else if (on) {
-    atomic_vec(dst_base + (size_t)e * stride, v);
+    for (int f = 0; f < F; f++) atomicAdd(p + f, x[f]);
   }
 }
 
 constexpr int kBwdWarps = 8;
+
+// Floats of shared memory each warp of backward_prim_kernel owns: phi rows, E
+// rows and its dW partial sums.
+__host__ __device__ inline int bwd_warp_floats(int D, int OMAX) { return 32 * (D + 1) + 32 * OMAX + OMAX * D; }
 
 // One warp per primitive, lane g = grid point g.  With dIn_p = W^T dpre_p
 // (backward.cu:608-619), every per-pair sum collapses onto O-wide vectors:
@@ -229,9 +209,10 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) backward_prim_kernel(Scene 
   float* W_s = smem;              // [D][OMAX]: W transposed
   float* dW_s = W_s + D * OMAX;   // [OMAX][D]
   float* db_s = dW_s + OMAX * D;  // [OMAX]
+  float* resf_s = db_s + OMAX;    // [L] level resolutions as float
   const int w = threadIdx.x >> 5;
   const uint32_t lane = threadIdx.x & 31;
-  float* phi_s = db_s + OMAX + w * (32 * DS + 32 * OMAX + OMAX * D);  // [32][DS]
+  float* phi_s = resf_s + L + w * bwd_warp_floats(D, OMAX);  // [32][DS]
   float* E_s = phi_s + 32 * DS;                                        // [32][OMAX]
   float* dWw = E_s + 32 * OMAX;  // [OMAX][D] this warp's dW partial sums; lane j owns columns j, j+32
   for (int i = (int)lane; i < OMAX * D; i += 32) dWw[i] = 0.0f;
@@ -242,9 +223,11 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) backward_prim_kernel(Scene 
     dW_s[i] = 0.0f;
   }
   for (int i = threadIdx.x; i < OMAX; i += blockDim.x) db_s[i] = 0.0f;
+  for (int i = threadIdx.x; i < L; i += blockDim.x) resf_s[i] = (float)sc.res[i];
   __syncthreads();
 
   const Stencil st = make_stencil(sc.genus);
+  const GridPt gpt = grid_point((int)lane < V ? (int)lane : 0, G, sc.gof);
   const uint32_t p0 = (uint32_t)__ldg(sc.primes), p1 = (uint32_t)__ldg(sc.primes + 1),
                  p2 = (uint32_t)__ldg(sc.primes + 2);
   float dbacc = 0.0f;
@@ -264,18 +247,19 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) backward_prim_kernel(Scene 
     const uint32_t n = g.rec_cnt[q] & ~kBwdDiffers;
     if (n == 0) continue;
     const size_t s0 = (size_t)q * V;
-    const uint32_t cm = __ballot_sync(0xffffffffu, lane < n && g.rec_flag[s0 + lane] != 0);
+    const uint32_t rp = lane < n ? g.rec_pix[s0 + lane] : 0u;
+    const uint32_t cm = __ballot_sync(0xffffffffu, rp != 0u);
     if (cm == 0) continue;
 
     const bool act = (int)lane < V;
     const float conf = act ? sc.conf[s0 + lane] : 0.0f;
     const float3 c = make_float3(sc.means[3 * q], sc.means[3 * q + 1], sc.means[3 * q + 2]);
-    const float3 pos = grid_pos(c, act ? (int)lane : 0, G, sc.step, sc.gof);
+    const float3 pos = grid_pos_rel(c, gpt.rel, sc.step);
     const float2 sb = project(pos, sc.proj, sc.W, sc.H, false);
     const int bx = pix_coord(sb.x), by = pix_coord(sb.y);
     const int bpix = (act && bx >= 0 && bx < sc.W && by >= 0 && by < sc.H) ? by * sc.W + bx : -1;
     const uint32_t posm = __ballot_sync(0xffffffffu, act && conf > 0.0f);
-    const float mag = act ? occ_mag(posm, lane, G, st) : 0.0f;
+    const float mag = act ? occ_mag(posm, gpt, G, st) : 0.0f;
     const float wE = (act && conf > 0.0f && mag > 1e-7f) ? fmul(conf, mag) : 0.0f;
 
     float v[OMAX], vA[OMAX];
@@ -287,9 +271,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) backward_prim_kernel(Scene 
       const int j = __ffs(m) - 1;
       m &= m - 1;
       const size_t slot = s0 + j;
-      const uint32_t key = g.rec_key[slot];
-      const uint32_t t = key >> 8;
-      const int ppx = (int)((t % sc.gx) * 16 + (key & 15u)), ppy = (int)((t / sc.gx) * 16 + ((key >> 4) & 15u));
+      const int ppix = (int)__shfl_sync(0xffffffffu, rp, j) - 1;  // pixel of this contribution
       float dpre[OMAX];
       const float4* src = reinterpret_cast<const float4*>(g.rec_dpre + slot * OMAX);
 #pragma unroll
@@ -297,16 +279,14 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) backward_prim_kernel(Scene 
         const float4 x = src[o4];
         dpre[4 * o4] = x.x; dpre[4 * o4 + 1] = x.y; dpre[4 * o4 + 2] = x.z; dpre[4 * o4 + 3] = x.w;
       }
-#pragma unroll
-      for (int o = 0; o < OMAX; o++)
-        if ((int)lane == o) dbacc += dpre[o];
-      const uint32_t inm = __ballot_sync(0xffffffffu, bpix == ppy * sc.W + ppx);
+      if ((int)lane < O) dbacc += g.rec_dpre[slot * OMAX + lane];
+      const uint32_t inm = __ballot_sync(0xffffffffu, bpix == ppix);
       if (((inm >> lane) & 1u) && wE != 0.0f) {
         hasE = true;
 #pragma unroll
         for (int o = 0; o < OMAX; o++) E_s[lane * OMAX + o] = fmul(wE, dpre[o]);
       }
-      const float gp = act ? occ_mag(inm, lane, G, st) : 0.0f;
+      const float gp = act ? occ_mag(inm, gpt, G, st) : 0.0f;
       if (gp > 1e-7f) {
         hasV = true;
         const bool doA = fabsf(fmul(gp, conf)) > 1e-9f;
@@ -322,69 +302,87 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) backward_prim_kernel(Scene 
     if (!__any_sync(0xffffffffu, hasE || hasV)) continue;
 
     // One pass over the levels: gather phi_g (for dconf and dW), scatter the table gradient.
-    float mlp[OMAX];
+    float2 mlp2[OMAX / 2];
 #pragma unroll
-    for (int o = 0; o < OMAX; o++) mlp[o] = 0.0f;
+    for (int o = 0; o < OMAX / 2; o++) mlp2[o] = make_float2(0.0f, 0.0f);
     float* phi_row = phi_s + lane * DS;
     const bool gather = hasE || hasV;
     const float3 nrm = hash_norm(pos);
+    const uint32_t amask = __ballot_sync(0xffffffffu, hasA);
+    const int afirst = amask ? __ffs(amask) - 1 : 0;
 #pragma unroll 1
     for (int l = 0; l < L; l++) {
-      const int res = __ldg(sc.res + l);
-      const bool hsh = __ldg(sc.do_hash + l) != 0;
-      int3 b;
-      float3 tt;
-      level_setup_n(nrm, res, b, tt);
+      const LevelCorners lc =
+          level_corners(nrm, __ldg(sc.res + l), resf_s[l], __ldg(sc.do_hash + l) != 0, p0, p1, p2, sc.T);
+      const uint32_t cmask = (gather || hasA) ? lc.mask : 0u;
       float acc[F], a[F];
 #pragma unroll
       for (int f = 0; f < F; f++) {
         acc[f] = 0.0f;
         // table coefficient of this level: conf_g * sum_o W[o][l*F+f] vA[o]
-        float sum = 0.0f;
-        const float* wr = W_s + (l * F + f) * OMAX;
+        float2 sum = make_float2(0.0f, 0.0f);
+        const float2* wr = reinterpret_cast<const float2*>(W_s + (l * F + f) * OMAX);
 #pragma unroll
-        for (int o = 0; o < OMAX; o++) sum += wr[o] * vA[o];
-        a[f] = conf * sum;
+        for (int o = 0; o < OMAX / 2; o++) sum = __ffma2_rn(wr[o], make_float2(vA[2 * o], vA[2 * o + 1]), sum);
+        a[f] = conf * (sum.x + sum.y);
       }
-      // Corners with a nonzero trilinear weight: an axis whose fraction is 0
-      // contributes only its lower corner.  Bit (dx + 2 dy + 4 dz).
-      const uint32_t mx = tt.x != 0.0f ? 0xffu : 0x55u, my = tt.y != 0.0f ? 0xffu : 0x33u,
-                     mz = tt.z != 0.0f ? 0xffu : 0x0fu;
-      const uint32_t cmask = (gather || hasA) ? (mx & my & mz) : 0u;
-      const int kmax = (int)__reduce_max_sync(0xffffffffu, (unsigned)__popc(cmask));
+      // Every lane with a table gradient on the same cell set (points clamped to
+      // the hashgrid box): sum per corner across the warp, one atomic per corner.
+      bool uni = false;
+      if (amask) {
+        const uint32_t m0 = __shfl_sync(0xffffffffu, cmask, afirst);
+        const uint32_t i0 = __shfl_sync(0xffffffffu, lc.ix0, afirst);
+        const uint32_t j0 = __shfl_sync(0xffffffffu, lc.iy0, afirst);
+        const uint32_t k0 = __shfl_sync(0xffffffffu, lc.iz0, afirst);
+        uni = __all_sync(0xffffffffu, !hasA || (cmask == m0 && lc.ix0 == i0 && lc.iy0 == j0 && lc.iz0 == k0)) &&
+              __popc(amask) > 1;
+      }
       const float* lvl = sc.table + (size_t)l * F;
-      for (int k = 0; k < kmax; k++) {
-        int e = -1;
-        float cw = 0.0f;
-        if (k < __popc(cmask)) {
-          const int cidx = __fns(cmask, 0, k + 1);
-          const int dx = cidx & 1, dy = (cidx >> 1) & 1, dz = cidx >> 2;
-          cw = (dx ? tt.x : 1.0f - tt.x) * (dy ? tt.y : 1.0f - tt.y) * (dz ? tt.z : 1.0f - tt.z);
-          e = cw != 0.0f ? corner_entry(b.x + dx, b.y + dy, b.z + dz, res, hsh, p0, p1, p2, sc.T, sc.Tmask) : -1;
-        }
-        if (gather && e >= 0) {
+      float* dst = dtable + (size_t)l * F;
+      uint32_t um = __reduce_or_sync(0xffffffffu, cmask);
+      while (um) {
+        const int k = __ffs(um) - 1;
+        um &= um - 1;
+        const bool on = (cmask >> k) & 1u;
+        const uint32_t e = on ? corner_index(lc, k, sc.T, sc.Tmask) : 0u;
+        const float cw = on ? corner_weight(lc, k) : 0.0f;
+        if (gather && on) {
           const FVec<F> x = load_feat<F>(lvl + (size_t)e * L * F);
 #pragma unroll
           for (int f = 0; f < F; f++) acc[f] += x.v[f] * cw;
         }
-        float val[F];
+        if (uni) {
+          if ((__shfl_sync(0xffffffffu, cmask, afirst) >> k) & 1u) {
+            float x[F];
 #pragma unroll
-        for (int f = 0; f < F; f++) val[f] = a[f] * cw;
-        scatter_add<F>(dtable + (size_t)l * F, e, hasA && e >= 0, val, (size_t)L * F, lane);
+            for (int f = 0; f < F; f++) {
+              float y = hasA ? a[f] * cw : 0.0f;
+#pragma unroll
+              for (int off = 16; off > 0; off >>= 1) y += __shfl_xor_sync(0xffffffffu, y, off);
+              x[f] = y;
+            }
+            if ((int)lane == afirst) atomic_vec<F>(dst + (size_t)e * L * F, x);
+          }
+        } else if (hasA && on) {
+          float x[F];
+#pragma unroll
+          for (int f = 0; f < F; f++) x[f] = a[f] * cw;
+          atomic_vec<F>(dst + (size_t)e * L * F, x);
+        }
       }
 #pragma unroll
       for (int f = 0; f < F; f++) {
         const float x = acc[f];
-        const float* wr = W_s + (l * F + f) * OMAX;
+        const float2* wr = reinterpret_cast<const float2*>(W_s + (l * F + f) * OMAX);
 #pragma unroll
-        for (int o = 0; o < OMAX; o++) mlp[o] += wr[o] * x;
+        for (int o = 0; o < OMAX / 2; o++) mlp2[o] = __ffma2_rn(wr[o], make_float2(x, x), mlp2[o]);
         if (hasE) phi_row[l * F + f] = x;
       }
     }
     if (act) {
       float dX = 0.0f;
 #pragma unroll
-      for (int o = 0; o < OMAX; o++) dX += v[o] * mlp[o];
+      for (int o = 0; o < OMAX / 2; o++) dX += v[2 * o] * mlp2[o].x + v[2 * o + 1] * mlp2[o].y;
       dconf[s0 + lane] = dX;
     }
     // dW += E_g (x) phi_g over the lanes with an E contribution.
@@ -423,7 +421,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) backward_prim_kernel(Scene 
 template <int F, int OMAX>
 void launch_prim_t(const Scene& sc, GeomState& g, float* dconf, float* dtable, float* dW, float* db, cudaStream_t s) {
   const int D = sc.L * F;
-  size_t smem = sizeof(float) * (2 * OMAX * D + OMAX + kBwdWarps * (32 * (D + 1) + 32 * OMAX + OMAX * D));
+  size_t smem = sizeof(float) * (2 * OMAX * D + OMAX + sc.L + kBwdWarps * bwd_warp_floats(D, OMAX));
   auto k = backward_prim_kernel<F, OMAX>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   cudaMemsetAsync(g.status + 5, 0, sizeof(uint32_t), s);
@@ -439,7 +437,7 @@ void launch_prim_t(const Scene& sc, GeomState& g, float* dconf, float* dtable, f
 void launch_backward(const Scene& sc, GeomState& g, const ImgState& im, const float* dL_dcolor, const float* dL_dfeat,
                      float* dconf, float* dtable, float* dW, float* db, cudaStream_t s) {
   const size_t N = (size_t)sc.W * sc.H;
-  cudaMemsetAsync(g.rec_flag, 0, (size_t)sc.P * sc.V, s);
+  cudaMemsetAsync(g.rec_pix, 0, (size_t)sc.P * sc.V * sizeof(uint32_t), s);
   const bool o16 = sc.O > 8;
   stage_begin(kStBwdPixel, s);
   if (N > 0) {

@@ -69,6 +69,11 @@ __device__ __forceinline__ int pix_coord(float s) {
   return (int)f;
 }
 
+// Grid point position from precomputed (float(coord) - gof) offsets (forward.cu:421-428).
+__device__ __forceinline__ float3 grid_pos_rel(float3 c, float3 rel, float step) {
+  return make_float3(fadd(c.x, fmul(rel.x, step)), fadd(c.y, fmul(rel.y, step)), fadd(c.z, fmul(rel.z, step)));
+}
+
 // Grid point position (forward.cu:416-428).
 __device__ __forceinline__ float3 grid_pos(float3 c, int g, int G, float step, float gof) {
   int z = g / (G * G), rem = g % (G * G), y = rem / G, x = rem % G;
@@ -88,13 +93,28 @@ __device__ __forceinline__ float3 hash_norm(float3 pos) {
                      fmaxf(0.0f, fminf(1.0f, __fdiv_rn(fsub(pos.z, -1.3f), 2.6f))));
 }
 
+// floor of x for 0 <= x < 2^23 on the FMA and integer pipes: adding 2^23 with
+// round-down leaves 2^23 + floor(x) exactly, so the integer floor is its bit
+// pattern minus that of 2^23 and the float floor is exact as well.  Equal to
+// floorf(x) and (int)floorf(x) on that range.
+__device__ __forceinline__ void floor_small(float x, int& i, float& f) {
+  const float y = __fadd_rd(x, 8388608.0f);
+  i = __float_as_int(y) - 0x4b000000;
+  f = fsub(y, 8388608.0f);
+}
+
 // Hashgrid level set-up (hashgrid.h:237-242): integer base corner and fractions.
-__device__ __forceinline__ void level_setup_n(float3 n, int res, int3& b, float3& t) {
-  float rf = (float)res;
+// n is in [0, 1] and res < 2^23, so every product is in [0, 2^23).
+__device__ __forceinline__ void level_setup_nf(float3 n, float rf, int3& b, float3& t) {
   float px = fmul(n.x, rf), py = fmul(n.y, rf), pz = fmul(n.z, rf);
-  float fx = floorf(px), fy = floorf(py), fz = floorf(pz);
-  b = make_int3((int)fx, (int)fy, (int)fz);
+  float fx, fy, fz;
+  floor_small(px, b.x, fx);
+  floor_small(py, b.y, fy);
+  floor_small(pz, b.z, fz);
   t = make_float3(fsub(px, fx), fsub(py, fy), fsub(pz, fz));
+}
+__device__ __forceinline__ void level_setup_n(float3 n, int res, int3& b, float3& t) {
+  level_setup_nf(n, (float)res, b, t);
 }
 
 __device__ __forceinline__ void level_setup(float3 pos, int res, int3& b, float3& t) {

@@ -24,14 +24,16 @@ namespace {
 constexpr int kFeatWarps = 8;
 
 template <int F, int OMAX>
-__global__ void __launch_bounds__(kFeatWarps * 32) features_kernel(Scene sc, GeomState g) {
+__global__ void __launch_bounds__(kFeatWarps * 32, 4) features_kernel(Scene sc, GeomState g) {
   extern __shared__ float smem[];
   const int D = sc.L * F, O = sc.O, V = sc.V, G = sc.G;
   float* W_s = smem;                       // [D][OMAX] (transposed for broadcast reads)
   float* b_s = W_s + D * OMAX;             // [OMAX]
+  float* resf_s = b_s + OMAX;              // [L] level resolutions as float
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* c_s = b_s + OMAX + w * (32 * OMAX + 32);  // [32][OMAX]
-  float* mag_s = c_s + 32 * OMAX;                   // [32]
+  float* c_s = resf_s + sc.L + w * (32 * OMAX + 32);  // [32][OMAX]
+  float* mag_s = c_s + 32 * OMAX;                      // [32]
+  for (int i = threadIdx.x; i < sc.L; i += blockDim.x) resf_s[i] = (float)sc.res[i];
 
   for (int i = threadIdx.x; i < D * OMAX; i += blockDim.x) {
     int d = i / OMAX, o = i % OMAX;
@@ -41,6 +43,7 @@ __global__ void __launch_bounds__(kFeatWarps * 32) features_kernel(Scene sc, Geo
   __syncthreads();
 
   const Stencil st = make_stencil(sc.genus);
+  const GridPt gp = grid_point(lane < V ? lane : 0, G, sc.gof);
   const uint32_t lt_mask = (1u << lane) - 1;
   const int OP = OMAX;
   const int nwarps = gridDim.x * kFeatWarps;
@@ -54,20 +57,20 @@ __global__ void __launch_bounds__(kFeatWarps * 32) features_kernel(Scene sc, Geo
     const float2 m2 = make_float2(g.means2D[2 * q], g.means2D[2 * q + 1]);
     // getRect with the same float arithmetic as preprocess (auxiliary.h:55-65).
     const float rf = (float)r;
-    const unsigned x0 = min(sc.gx, (unsigned)max(0, (int)__fdiv_rn(fsub(m2.x, rf), 16.0f)));
-    const unsigned y0 = min(sc.gy, (unsigned)max(0, (int)__fdiv_rn(fsub(m2.y, rf), 16.0f)));
-    const unsigned x1 = min(sc.gx, (unsigned)max(0, (int)__fdiv_rn(fsub(fadd(fadd(m2.x, rf), 16.0f), 1.0f), 16.0f)));
-    const unsigned y1 = min(sc.gy, (unsigned)max(0, (int)__fdiv_rn(fsub(fadd(fadd(m2.y, rf), 16.0f), 1.0f), 16.0f)));
+    const unsigned x0 = min(sc.gx, (unsigned)max(0, (int)fmul(fsub(m2.x, rf), 0.0625f)));
+    const unsigned y0 = min(sc.gy, (unsigned)max(0, (int)fmul(fsub(m2.y, rf), 0.0625f)));
+    const unsigned x1 = min(sc.gx, (unsigned)max(0, (int)fmul(fsub(fadd(fadd(m2.x, rf), 16.0f), 1.0f), 0.0625f)));
+    const unsigned y1 = min(sc.gy, (unsigned)max(0, (int)fmul(fsub(fadd(fadd(m2.y, rf), 16.0f), 1.0f), 0.0625f)));
 
     const bool act = lane < V;
     const float conf = act ? sc.conf[(size_t)q * V + lane] : 0.0f;
-    const float3 pos = grid_pos(c, act ? lane : 0, G, sc.step, sc.gof);
+    const float3 pos = grid_pos_rel(c, gp.rel, sc.step);
     const float2 sf = project(pos, sc.proj, sc.W, sc.H, true);
     const float2 sb = project(pos, sc.proj, sc.W, sc.H, false);
     const int fx = pix_coord(sf.x), fy = pix_coord(sf.y);
     const bool differs = __any_sync(0xffffffffu, act && (fx != pix_coord(sb.x) || fy != pix_coord(sb.y)));
     const uint32_t posm = __ballot_sync(0xffffffffu, act && conf > 0.0f);
-    const float mag = act ? occ_mag(posm, lane, G, st) : 0.0f;
+    const float mag = act ? occ_mag(posm, gp, G, st) : 0.0f;
     const bool inside = fx >= 0 && fx < sc.W && fy >= 0 && fy < sc.H;
     const unsigned tx = (unsigned)fx >> 4, ty = (unsigned)fy >> 4;
     const bool vpt = act && conf > 0.0f && inside && tx >= x0 && tx < x1 && ty >= y0 && ty < y1;
@@ -76,29 +79,33 @@ __global__ void __launch_bounds__(kFeatWarps * 32) features_kernel(Scene sc, Geo
     float cvec[OMAX];
 #pragma unroll
     for (int o = 0; o < OMAX; o++) cvec[o] = 0.0f;
-    if (need) {
+    if (__any_sync(0xffffffffu, need)) {
       // Linear layer accumulated level by level: mlp[o] = sum_i W[o][i] phi[i], i ascending.
-      float mlp[OMAX];
+      float2 mlp[OMAX / 2];  // output pairs, two fused multiply-adds per instruction
 #pragma unroll
-      for (int o = 0; o < OMAX; o++) mlp[o] = 0.0f;
-      for_each_level<F>(sc, pos, [&](int l, const float* phi, int3, float3, int, bool) {
+      for (int o = 0; o < OMAX / 2; o++) mlp[o] = make_float2(0.0f, 0.0f);
+      for_each_level<F>(sc, resf_s, pos, need, [&](int l, const float* phi) {
+        if (!need) return;
 #pragma unroll
         for (int f = 0; f < F; f++) {
-          const float x = phi[f];
+          const float2 x = make_float2(phi[f], phi[f]);
           const float4* wr = reinterpret_cast<const float4*>(W_s + (l * F + f) * OMAX);
 #pragma unroll
           for (int o4 = 0; o4 < OMAX / 4; o4++) {
             const float4 ww = wr[o4];
-            mlp[4 * o4 + 0] += ww.x * x;
-            mlp[4 * o4 + 1] += ww.y * x;
-            mlp[4 * o4 + 2] += ww.z * x;
-            mlp[4 * o4 + 3] += ww.w * x;
+            mlp[2 * o4] = __ffma2_rn(make_float2(ww.x, ww.y), x, mlp[2 * o4]);
+            mlp[2 * o4 + 1] = __ffma2_rn(make_float2(ww.z, ww.w), x, mlp[2 * o4 + 1]);
           }
         }
       });
-      const float wgt = fmul(conf, mag);
+      if (need) {
+        const float wgt = fmul(conf, mag);
 #pragma unroll
-      for (int o = 0; o < OMAX; o++) cvec[o] = fmul(mlp[o], wgt);
+        for (int o = 0; o < OMAX / 2; o++) {
+          cvec[2 * o] = fmul(mlp[o].x, wgt);
+          cvec[2 * o + 1] = fmul(mlp[o].y, wgt);
+        }
+      }
     }
 #pragma unroll
     for (int o = 0; o < OMAX; o++) c_s[lane * OMAX + o] = cvec[o];
@@ -157,7 +164,7 @@ __global__ void __launch_bounds__(kFeatWarps * 32) features_kernel(Scene sc, Geo
 template <int F, int OMAX>
 void launch_features_t(const Scene& sc, GeomState& g, cudaStream_t s) {
   const int D = sc.L * F;
-  size_t smem = sizeof(float) * (D * OMAX + OMAX + kFeatWarps * (32 * OMAX + 32));
+  size_t smem = sizeof(float) * (D * OMAX + OMAX + sc.L + kFeatWarps * (32 * OMAX + 32));
   auto k = features_kernel<F, OMAX>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   int blocks = (sc.P + kFeatWarps - 1) / kFeatWarps;

@@ -58,7 +58,7 @@ struct GeomState {
   uint32_t* rec_cnt;         // [P] record count | kBwdDiffers
   uint32_t* rec_key;         // [P*V] tile*256 + pixel-in-tile, sorted per primitive
   float* rec_props;          // [P*V*O] activated colour, features, density per record
-  uint8_t* rec_flag;         // [P*V] record is a contributor (written by the backward)
+  uint32_t* rec_pix;         // [P*V] pixel + 1 of a contributing record, 0 otherwise (backward)
   float* rec_dpre;           // [P*V*O] dL/d(pre-activation) per contributing record
   SortTemp sort;
   size_t bytes;

@@ -22,12 +22,40 @@ __host__ __device__ inline Stencil make_stencil(int genus) {
   return s;
 }
 
+// Coordinates of grid point g (flat index z*G^2 + y*G + x) and its offset from the
+// cube centre in grid steps, formed once per thread.
+struct GridPt {
+  int g, x, y, z;
+  float3 rel;
+};
+__device__ __forceinline__ GridPt grid_point(int g, int G, float gof) {
+  GridPt p;
+  p.g = g;
+  p.z = g / (G * G);
+  const int rem = g % (G * G);
+  p.y = rem / G;
+  p.x = rem % G;
+  p.rel = make_float3(fsub((float)p.x, gof), fsub((float)p.y, gof), fsub((float)p.z, gof));
+  return p;
+}
+
 // |d/dx| + |d/dy| + |d/dz| of an occupancy given as a bit per grid point
 // (bit g set = grid point g occupied).  With conf>0 bits this is the forward's
 // stencil (forward.cu:557-611); with "screen point in this pixel" bits it is the
 // backward's (backward.cu:654-689).  Requires V <= 32.
-__device__ __forceinline__ float occ_mag(uint32_t occ, int g, int G, const Stencil& st) {
-  int z = g / (G * G), rem = g % (G * G), y = rem / G, x = rem % G, off = (st.S - 1) / 2;
+__device__ __forceinline__ float occ_mag(uint32_t occ, const GridPt& p, int G, const Stencil& st) {
+  const int g = p.g, x = p.x, y = p.y, z = p.z;
+  if (st.S == 3) {
+    // Taps (-1/2, 0, 1/2): each axis term is +-1/2 exactly when one of the two
+    // in-range neighbours is occupied, so the float sum is 0.5 * count (0..1.5).
+    const int GG = G * G;
+    const uint32_t xm = x > 0 ? (occ >> (g - 1)) & 1u : 0u, xp = x + 1 < G ? (occ >> (g + 1)) & 1u : 0u;
+    const uint32_t ym = y > 0 ? (occ >> (g - G)) & 1u : 0u, yp = y + 1 < G ? (occ >> (g + G)) & 1u : 0u;
+    const uint32_t zm = z > 0 ? (occ >> (g - GG)) & 1u : 0u, zp = z + 1 < G ? (occ >> (g + GG)) & 1u : 0u;
+    const uint32_t n = (xm ^ xp) + (ym ^ yp) + (zm ^ zp);
+    return (n & 1u ? 0.5f : 0.0f) + (n & 2u ? 1.0f : 0.0f);
+  }
+  const int off = (st.S - 1) / 2;
   float gx = 0.0f, gy = 0.0f, gz = 0.0f;
   for (int s = 0; s < st.S; s++) {
     int r = s - off, n;
@@ -39,6 +67,9 @@ __device__ __forceinline__ float occ_mag(uint32_t occ, int g, int G, const Stenc
     if (n >= 0 && n < G && ((occ >> (n * G * G + y * G + x)) & 1u)) gz = fadd(gz, st.c[s]);
   }
   return fadd(fadd(fabsf(gx), fabsf(gy)), fabsf(gz));
+}
+__device__ __forceinline__ float occ_mag(uint32_t occ, int g, int G, const Stencil& st) {
+  return occ_mag(occ, grid_point(g, G, 0.0f), G, st);
 }
 
 // F contiguous table floats of one (entry, level).
@@ -67,50 +98,102 @@ __device__ __forceinline__ FVec<F> load_feat(const float* __restrict__ p) {
   return r;
 }
 
+// The eight corners of one point at one hashgrid level (hashgrid.h:237-287).
+// Corner k has offsets dx = k >> 2, dy = (k >> 1) & 1, dz = k & 1, so ascending k
+// is the reference's dx, dy, dz nesting order.  Per-axis weights and index terms
+// are formed once; `mask` has bit k set for every corner whose weight is not
+// trivially zero (an axis with fraction 0 keeps only its lower corner) and whose
+// table index is valid.  A skipped corner would add table * 0, which leaves a
+// sum of finite values unchanged.
+struct LevelCorners {
+  float wx0, wx1, wy0, wy1, wz0, wz1;
+  uint32_t ix0, ix1, iy0, iy1, iz0, iz1;
+  uint32_t mask;
+  bool hsh;
+};
+
+__device__ __forceinline__ LevelCorners level_corners(float3 nrm, int res, float resf, bool hsh, uint32_t p0,
+                                                      uint32_t p1, uint32_t p2, uint32_t T) {
+  LevelCorners c;
+  int3 b;
+  float3 t;
+  level_setup_nf(nrm, resf, b, t);
+  c.hsh = hsh;
+  c.wx0 = 1.0f - t.x; c.wx1 = t.x;
+  c.wy0 = 1.0f - t.y; c.wy1 = t.y;
+  c.wz0 = 1.0f - t.z; c.wz1 = t.z;
+  uint32_t mx = t.x != 0.0f ? 3u : 1u, my = t.y != 0.0f ? 3u : 1u, mz = t.z != 0.0f ? 3u : 1u;
+  if (hsh) {
+    c.ix0 = (uint32_t)b.x * p0; c.ix1 = (uint32_t)(b.x + 1) * p0;
+    c.iy0 = (uint32_t)b.y * p1; c.iy1 = (uint32_t)(b.y + 1) * p1;
+    c.iz0 = (uint32_t)b.z * p2; c.iz1 = (uint32_t)(b.z + 1) * p2;
+  } else {
+    // dense grid: index z*res^2 + y*res + x (uint32, as the reference), in range only
+    const uint32_t r = (uint32_t)res;
+    c.ix0 = (uint32_t)b.x; c.ix1 = (uint32_t)(b.x + 1);
+    c.iy0 = (uint32_t)b.y * r; c.iy1 = (uint32_t)(b.y + 1) * r;
+    c.iz0 = (uint32_t)b.z * r * r; c.iz1 = (uint32_t)(b.z + 1) * r * r;
+    mx &= (b.x >= 0 && b.x < res ? 1u : 0u) | (b.x + 1 >= 0 && b.x + 1 < res ? 2u : 0u);
+    my &= (b.y >= 0 && b.y < res ? 1u : 0u) | (b.y + 1 >= 0 && b.y + 1 < res ? 2u : 0u);
+    mz &= (b.z >= 0 && b.z < res ? 1u : 0u) | (b.z + 1 >= 0 && b.z + 1 < res ? 2u : 0u);
+  }
+  uint32_t m = ((mx & 1u) ? 0x0fu : 0u) | ((mx & 2u) ? 0xf0u : 0u);
+  m &= ((my & 1u) ? 0x33u : 0u) | ((my & 2u) ? 0xccu : 0u);
+  m &= ((mz & 1u) ? 0x55u : 0u) | ((mz & 2u) ? 0xaau : 0u);
+  if (!hsh) {
+    uint32_t mm = m;
+    while (mm) {
+      const int k = __ffs(mm) - 1;
+      mm &= mm - 1;
+      if (((k & 4) ? c.ix1 : c.ix0) + ((k & 2) ? c.iy1 : c.iy0) + ((k & 1) ? c.iz1 : c.iz0) >= T) m &= ~(1u << k);
+    }
+  }
+  c.mask = m;
+  return c;
+}
+
+// Table entry and trilinear weight ((wx * wy) * wz, hashgrid.h:253) of corner k.
+__device__ __forceinline__ uint32_t corner_index(const LevelCorners& c, int k, uint32_t T, uint32_t Tmask) {
+  const uint32_t x = (k & 4) ? c.ix1 : c.ix0, y = (k & 2) ? c.iy1 : c.iy0, z = (k & 1) ? c.iz1 : c.iz0;
+  if (c.hsh) {
+    const uint32_t h = x ^ y ^ z;
+    return Tmask ? (h & Tmask) : (h % T);
+  }
+  return x + y + z;
+}
+__device__ __forceinline__ float corner_weight(const LevelCorners& c, int k) {
+  return ((k & 4) ? c.wx1 : c.wx0) * ((k & 2) ? c.wy1 : c.wy0) * ((k & 1) ? c.wz1 : c.wz0);
+}
+
 // Trilinear hashgrid features of one point, level by level (hashgrid.h:207-299).
-// For each level, fn(l, acc) receives the F interpolated features.  Corners
-// are visited dx, dy, dz as the reference does; corners whose trilinear weight
-// is exactly zero are skipped (their product with a finite table value is
-// zero, so the sum is unchanged), which is most corners of points clamped to
-// the faces of the hashgrid box.
+// For each level, fn(l, acc) receives the F interpolated features.  `on` lanes
+// gather; the warp walks the union of the lanes' active corners in ascending
+// order, so a warp of points clamped to one face of the hashgrid box makes one
+// pass per level instead of eight.  Must be called by the whole warp.
 template <int F, typename Fn>
-__device__ __forceinline__ void for_each_level(const Scene& sc, float3 pos, Fn&& fn) {
+__device__ __forceinline__ void for_each_level(const Scene& sc, const float* resf, float3 pos, bool on, Fn&& fn) {
   const uint32_t p0 = (uint32_t)__ldg(sc.primes), p1 = (uint32_t)__ldg(sc.primes + 1),
                  p2 = (uint32_t)__ldg(sc.primes + 2);
   const float3 nrm = hash_norm(pos);
-#pragma unroll 2
   for (int l = 0; l < sc.L; l++) {
-    const int res = __ldg(sc.res + l);
-    const bool hsh = __ldg(sc.do_hash + l) != 0;
-    int3 b;
-    float3 t;
-    level_setup_n(nrm, res, b, t);
+    const LevelCorners c = level_corners(nrm, __ldg(sc.res + l), resf[l], __ldg(sc.do_hash + l) != 0, p0, p1, p2, sc.T);
+    const uint32_t mine = on ? c.mask : 0u;
     float acc[F];
 #pragma unroll
     for (int f = 0; f < F; f++) acc[f] = 0.0f;
     const float* lvl = sc.table + (size_t)l * F;
+    uint32_t um = __reduce_or_sync(0xffffffffu, mine);
+    while (um) {
+      const int k = __ffs(um) - 1;
+      um &= um - 1;
+      if ((mine >> k) & 1u) {
+        const float w = corner_weight(c, k);
+        const FVec<F> v = load_feat<F>(lvl + (size_t)corner_index(c, k, sc.T, sc.Tmask) * sc.L * F);
 #pragma unroll
-    for (int dx = 0; dx < 2; dx++) {
-      const float wx = dx == 0 ? 1.0f - t.x : t.x;
-#pragma unroll
-      for (int dy = 0; dy < 2; dy++) {
-        const float wy = dy == 0 ? 1.0f - t.y : t.y;
-#pragma unroll
-        for (int dz = 0; dz < 2; dz++) {
-          const float wz = dz == 0 ? 1.0f - t.z : t.z;
-          const float w = wx * wy * wz;
-          if (w != 0.0f) {
-            const int e = corner_entry(b.x + dx, b.y + dy, b.z + dz, res, hsh, p0, p1, p2, sc.T, sc.Tmask);
-            if (e >= 0) {
-              const FVec<F> v = load_feat<F>(lvl + (size_t)e * sc.L * F);
-#pragma unroll
-              for (int f = 0; f < F; f++) acc[f] += v.v[f] * w;
-            }
-          }
-        }
+        for (int f = 0; f < F; f++) acc[f] += v.v[f] * w;
       }
     }
-    fn(l, acc, b, t, res, hsh);
+    fn(l, acc);
   }
 }
 
