@@ -59,7 +59,7 @@ def _declare(l):
     l.vio_sort.argtypes = [u64, vp, vp, vp, vp, i]
     l.vio_ranges.argtypes = [u64, vp, vp]
     l.vio_mark_visible.argtypes = [i, vp, vp, vp]
-    l.vio_render.argtypes = [ctypes.POINTER(Params), vp, vp, vp, i, vp, vp, vp, vp, vp, vp, vp]
+    l.vio_render.argtypes = [ctypes.POINTER(Params), vp, vp, vp, i, vp, vp, vp, vp, vp, vp, vp, vp]
     l.vio_backward.argtypes = [ctypes.POINTER(Params), vp, vp, u64, vp, i, vp, vp, vp, vp, vp,
                                vp, vp, vp, vp]
 
@@ -184,12 +184,14 @@ def render(s, binned, tile_mask=None, threads=0):
         n_contrib=np.zeros(N, np.int32),
         contrib_idx=np.full(N * K, -1, np.int32),
         delta_t=np.zeros(N * K, np.float32),
+        skips=np.zeros(N, np.int32),
     )
     tm = None if tile_mask is None else _c(tile_mask, np.uint8)
     p = s.params()
     lib().vio_render(ctypes.byref(p), _p(binned["ranges"]), _p(binned["point_list"]), _p(tm), int(threads),
                      _p(out["out_color"]), _p(out["out_features"]), _p(out["visibility"]),
-                     _p(out["final_T"]), _p(out["n_contrib"]), _p(out["contrib_idx"]), _p(out["delta_t"]))
+                     _p(out["final_T"]), _p(out["n_contrib"]), _p(out["contrib_idx"]), _p(out["delta_t"]),
+                     _p(out["skips"]))
     return out
 
 

@@ -397,10 +397,15 @@ static float sigm(float x) { return 1.0f / (1.0f + expf(-x)); }
 /* ------------------------------------------------------------------------ */
 /* R5: render (forward.cu:146-792), per tile, program order                   */
 /* ------------------------------------------------------------------------ */
+/* skips (optional, per pixel): entries an active pixel visited while not done
+ * that no grid point covers (occupancy sum < 1e-7).  At exactly these events
+ * the reference kernel's thread leaves the loop body before the CTA barrier at
+ * forward.cu:715 (forward.cu:629-631), so a scene with zero skips is one on
+ * which every reference thread takes every barrier. */
 void vio_render(const vio_params *p, const uint32_t *ranges, const uint32_t *point_list,
                 const uint8_t *tile_mask, int nthreads,
                 float *out_color, float *out_feat, float *vis,
-                float *final_T, int32_t *n_contrib, int32_t *contrib_idx, float *delta_t) {
+                float *final_T, int32_t *n_contrib, int32_t *contrib_idx, float *delta_t, int32_t *skips) {
     int W = p->W, H = p->H, G = p->G, V = G * G * G, D = p->L * p->F, O = 3 + p->Fout + 1;
     int K = p->K;
     unsigned gxn = (W + TILE - 1) / TILE, gyn = (H + TILE - 1) / TILE;
@@ -461,7 +466,10 @@ void vio_render(const vio_params *p, const uint32_t *ranges, const uint32_t *poi
                             for (int o = 0; o < O; o++) acc[o] += mlp[(size_t)g * O + o] * w;
                         }
                     }
-                    if (ogs < 1e-7f) continue;
+                    if (ogs < 1e-7f) {
+                        if (skips) skips[(size_t)py * W + px]++;
+                        continue;
+                    }
                     for (int o = 0; o < O; o++) {
                         acc[o] += p->bl[o];
                         acc[o] = o < O - 1 ? sigm(acc[o]) : expf(acc[o]);
