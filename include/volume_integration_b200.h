@@ -105,6 +105,25 @@ size_t vi_sort_pairs_temp_bytes(uint64_t n, int begin_bit, int end_bit);
 int vi_sort_pairs(uint64_t* keys_in, uint32_t* vals_in, uint64_t* keys_out, uint32_t* vals_out, uint64_t n,
                   int begin_bit, int end_bit, void* temp, size_t temp_bytes, void* stream);
 
+/*
+ * vi_sort_pairs for callers that must not allocate device memory (hosts that own
+ * every byte of device memory, or that cannot take the implicit device-wide
+ * synchronisation of cudaMalloc/cudaFree mid-frame).  No counterpart in the
+ * reference.  Same contract as vi_sort_pairs except that the sort's scratch lives
+ * in a fixed 3 MiB device array inside libvi_b200.so (held by every GPU that loads
+ * the library until the process exits), so no temp buffer is passed:
+ *   - n <= VI_SORT_NOALLOC_MAX_KEYS; larger n returns VI_ERR_INVALID_ARGUMENT;
+ *   - keys_in/vals_in are clobbered; the sorted pairs land in keys_out/vals_out;
+ *   - the first call on a device looks up the array's device address (make that
+ *     first call before any stream capture);
+ *   - every call uses the same array: calls that overlap on the GPU (other
+ *     streams, other threads) race and must be serialised by the caller.
+ * Calls no cudaMalloc, cudaFree or allocating library routine.
+ */
+#define VI_SORT_NOALLOC_MAX_KEYS (1u << 20)
+int vi_sort_pairs_noalloc(uint64_t* keys_in, uint32_t* vals_in, uint64_t* keys_out, uint32_t* vals_out, uint64_t n,
+                          int begin_bit, int end_bit, void* stream);
+
 /* Number of key bits the reference sorts on: 32 + getHigherMsb(tiles)
  * (reference: cuda_integrator/integrator_impl.cu:47-62, :341). */
 int vi_sort_end_bit(uint32_t num_tiles);

@@ -224,6 +224,10 @@ int check(cudaStream_t s, int debug, const char* where, const uint32_t* status) 
 }
 
 }  // namespace
+
+// Records a message for vi_last_error() and returns code (for other translation units).
+int set_error(int code, const char* msg) { return fail(code, "%s", msg); }
+
 }  // namespace vi
 
 using namespace vi;
