@@ -158,6 +158,7 @@ def run_ours(args):
     device = torch.device("cuda", torch.cuda.current_device())
     import volume_integration as vi
     from volume_integration import _C
+    from volume_integration.distributed import allreduce_gradients
 
     means, conf, s, dc, df = workload(args.config, rank, world, device)
     P = means.shape[0]
@@ -170,10 +171,7 @@ def run_ours(args):
     def step(m, c, t, w, b):
         oc, of, vis = vi.integrate_primitives(m, c, t, w, b, s)
         grads = torch.autograd.grad([oc, of], [c, t, w, b], [dc, df])
-        if world > 1:
-            works = [dist.all_reduce(g, async_op=True) for g in grads]
-            for wk in works:
-                wk.wait()
+        allreduce_gradients(grads)  # sum over ranks (no-op with one rank)
         return oc, of, vis, grads
 
     # workload statistics for the roofline (one forward, outside timing)
@@ -263,6 +261,7 @@ def run_ours(args):
 def run_e2e(args, vi, means, conf, s, dc, df, world, dist, device):
     """Same step through the public API with host inputs: pinned H2D copies of every
     input and D2H copies of the images and gradients inside the timed region."""
+    from volume_integration.distributed import allreduce_gradients
     host_in = [t.detach().cpu().pin_memory() for t in (means, conf, s.feature_table, s.linear_weights,
                                                       s.linear_bias, dc, df)]
     dev_in = [torch.empty_like(t, device=device) for t in host_in]
@@ -280,9 +279,7 @@ def run_e2e(args, vi, means, conf, s, dc, df, world, dist, device):
         b.requires_grad_(True)
         oc, of, vis = vi.integrate_primitives(m, c, t, w, b, s)
         grads = torch.autograd.grad([oc, of], [c, t, w, b], [gc, gf])
-        if dist is not None:
-            for g in grads:
-                dist.all_reduce(g)
+        allreduce_gradients(grads)
         res = [oc.detach(), of.detach(), vis.detach()] + list(grads)
         if outs is None:
             outs = [torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res]
