@@ -4,11 +4,14 @@
 // given (primitive, pixel) depends only on the primitive.
 //
 // One warp per primitive, lane g = grid point g (V = G^3 <= 32).  Per lane:
-// confidence, forward and backward screen positions, the conf>0 stencil
-// magnitude, hashgrid features (L levels x 8 corners) and the linear layer.
-// Lanes that land in the same pixel are then summed in grid-point order by the
-// lowest such lane, exactly the order of the reference's loop, and every pixel
-// whose occupancy sum passes the reference's 1e-7 test becomes one record:
+// confidence, forward and backward screen positions and the conf>0 stencil
+// magnitude.  The hashgrid features and the linear layer are then computed once
+// per distinct normalised position rather than once per grid point: lanes are
+// grouped by position, the (position, level) pairs are spread over the warp's
+// lanes, and the linear layer runs over (position, output) pairs.  Lanes that
+// land in the same pixel are summed in grid-point order by the lowest such lane,
+// exactly the order of the reference's loop, and every pixel whose occupancy sum
+// passes the reference's 1e-7 test becomes one record:
 //   key   = tile * 256 + pixel-in-tile (only tiles inside the primitive's rect)
 //   props = sigmoid(acc + b) for colour and features, exp(acc + b) for density.
 // Records of a primitive are stored sorted by key in slots [q*V, q*V + count).
@@ -23,21 +26,42 @@ namespace {
 
 constexpr int kFeatWarps = 8;
 
+__host__ __device__ inline int pad4(int x) { return (x + 3) & ~3; }
+// Shared memory: W [OMAX][DP] (rows of the linear layer, DP = pad4(D) + 4 to
+// spread rows over banks), bias, per-level resolution / hash flag, then per warp
+// phi [32][DP] (features of each position class), mlp [32][OMAX] (W phi of each
+// class), class positions [32] float4, and per-lane magnitude, weight and class.
+__host__ __device__ inline int feat_dp(int D) { return pad4(D) + 4; }
+__host__ __device__ inline int feat_head_floats(int D, int L, int OMAX) {
+  return OMAX * feat_dp(D) + OMAX + 3 * pad4(L);
+}
+__host__ __device__ inline int feat_warp_floats(int D, int OMAX) { return 32 * feat_dp(D) + 32 * OMAX + 4 * 32 + 3 * 32; }
+
 template <int F, int OMAX>
 __global__ void __launch_bounds__(kFeatWarps * 32, 4) features_kernel(Scene sc, GeomState g) {
-  extern __shared__ float smem[];
-  const int D = sc.L * F, O = sc.O, V = sc.V, G = sc.G;
-  float* W_s = smem;                       // [D][OMAX] (transposed for broadcast reads)
-  float* b_s = W_s + D * OMAX;             // [OMAX]
-  float* resf_s = b_s + OMAX;              // [L] level resolutions as float
+  extern __shared__ float4 smem4[];
+  float* smem = reinterpret_cast<float*>(smem4);
+  const int L = sc.L, D = L * F, DP = feat_dp(D), O = sc.O, V = sc.V, G = sc.G;
+  float* W_s = smem;                                       // [OMAX][DP]
+  float* b_s = W_s + OMAX * DP;                            // [OMAX]
+  float* resf_s = b_s + OMAX;                              // [L] level resolutions as float
+  int* res_s = reinterpret_cast<int*>(resf_s + pad4(L));   // [L]
+  int* hash_s = res_s + pad4(L);                           // [L]
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* c_s = resf_s + sc.L + w * (32 * OMAX + 32);  // [32][OMAX]
-  float* mag_s = c_s + 32 * OMAX;                      // [32]
-  for (int i = threadIdx.x; i < sc.L; i += blockDim.x) resf_s[i] = (float)sc.res[i];
-
-  for (int i = threadIdx.x; i < D * OMAX; i += blockDim.x) {
-    int d = i / OMAX, o = i % OMAX;
-    W_s[i] = o < O ? sc.Wl[o * D + d] : 0.0f;
+  float* phi_s = smem + feat_head_floats(D, L, OMAX) + w * feat_warp_floats(D, OMAX);  // [32][DP]
+  float* mlp_s = phi_s + 32 * DP;                                                    // [32][OMAX]
+  float4* npos_s = reinterpret_cast<float4*>(mlp_s + 32 * OMAX);                     // [32]
+  float* mag_s = reinterpret_cast<float*>(npos_s + 32);                              // [32]
+  float* wgt_s = mag_s + 32;                                                         // [32]
+  int* cls_s = reinterpret_cast<int*>(wgt_s + 32);                                   // [32]
+  for (int i = threadIdx.x; i < L; i += blockDim.x) {
+    res_s[i] = sc.res[i];
+    resf_s[i] = (float)sc.res[i];
+    hash_s[i] = sc.do_hash[i];
+  }
+  for (int i = threadIdx.x; i < OMAX * DP; i += blockDim.x) {
+    const int o = i / DP, d = i % DP;
+    W_s[i] = o < O && d < D ? sc.Wl[o * D + d] : 0.0f;
   }
   for (int i = threadIdx.x; i < OMAX; i += blockDim.x) b_s[i] = i < O ? sc.bl[i] : 0.0f;
   __syncthreads();
@@ -45,6 +69,9 @@ __global__ void __launch_bounds__(kFeatWarps * 32, 4) features_kernel(Scene sc, 
   const Stencil st = make_stencil(sc.genus);
   const GridPt gp = grid_point(lane < V ? lane : 0, G, sc.gof);
   const uint32_t lt_mask = (1u << lane) - 1;
+  const uint32_t p0 = (uint32_t)__ldg(sc.primes), p1 = (uint32_t)__ldg(sc.primes + 1),
+                 p2 = (uint32_t)__ldg(sc.primes + 2);
+  const uint32_t stride = (uint32_t)D;
   const int OP = OMAX;
   const int nwarps = gridDim.x * kFeatWarps;
   for (int q = blockIdx.x * kFeatWarps + w; q < sc.P; q += nwarps) {
@@ -76,39 +103,56 @@ __global__ void __launch_bounds__(kFeatWarps * 32, 4) features_kernel(Scene sc, 
     const bool vpt = act && conf > 0.0f && inside && tx >= x0 && tx < x1 && ty >= y0 && ty < y1;
     const bool need = vpt && mag > 1e-7f;
 
-    float cvec[OMAX];
-#pragma unroll
-    for (int o = 0; o < OMAX; o++) cvec[o] = 0.0f;
     if (__any_sync(0xffffffffu, need)) {
-      // Linear layer accumulated level by level: mlp[o] = sum_i W[o][i] phi[i], i ascending.
-      float2 mlp[OMAX / 2];  // output pairs, two fused multiply-adds per instruction
+      // Features of each distinct position: items (class u, level l) over the lanes.
+      const PosClasses pc = pos_classes(hash_norm(pos), need);
+      if (need && (pc.peers & lt_mask) == 0) {
+        const float3 n = hash_norm(pos);
+        npos_s[pc.cls] = make_float4(n.x, n.y, n.z, 0.0f);
+      }
+      __syncwarp();
+      ItemWalk it(L);
+      for (int base = 0; base < pc.U * L; base += 32, it.next()) {
+        if (it.u < pc.U) {
+          const float4 n4 = npos_s[it.u];
+          const LevelCorners lc = level_corners(make_float3(n4.x, n4.y, n4.z), res_s[it.l], resf_s[it.l],
+                                                hash_s[it.l] != 0, p0, p1, p2, sc.T);
+          float acc[F];
 #pragma unroll
-      for (int o = 0; o < OMAX / 2; o++) mlp[o] = make_float2(0.0f, 0.0f);
-      for_each_level<F>(sc, resf_s, pos, need, [&](int l, const float* phi) {
-        if (!need) return;
+          for (int f = 0; f < F; f++) acc[f] = 0.0f;
+          const float* lvl = sc.table + (size_t)it.l * F;
+          if (sc.Tmask)
+            gather_level<F, true>(lc, lvl, stride, sc.T, sc.Tmask, acc);
+          else
+            gather_level<F, false>(lc, lvl, stride, sc.T, sc.Tmask, acc);
 #pragma unroll
-        for (int f = 0; f < F; f++) {
-          const float2 x = make_float2(phi[f], phi[f]);
-          const float4* wr = reinterpret_cast<const float4*>(W_s + (l * F + f) * OMAX);
-#pragma unroll
-          for (int o4 = 0; o4 < OMAX / 4; o4++) {
-            const float4 ww = wr[o4];
-            mlp[2 * o4] = __ffma2_rn(make_float2(ww.x, ww.y), x, mlp[2 * o4]);
-            mlp[2 * o4 + 1] = __ffma2_rn(make_float2(ww.z, ww.w), x, mlp[2 * o4 + 1]);
-          }
-        }
-      });
-      if (need) {
-        const float wgt = fmul(conf, mag);
-#pragma unroll
-        for (int o = 0; o < OMAX / 2; o++) {
-          cvec[2 * o] = fmul(mlp[o].x, wgt);
-          cvec[2 * o + 1] = fmul(mlp[o].y, wgt);
+          for (int f = 0; f < F; f++) phi_s[it.u * DP + it.l * F + f] = acc[f];
         }
       }
+      __syncwarp();
+      // Linear layer per class: mlp[u][o] = sum_i W[o][i] phi_u[i], i ascending.
+      for (int base = 0; base < pc.U * OMAX; base += 32) {
+        const int item = base + lane, u = item / OMAX, o = item % OMAX;
+        if (u < pc.U) {
+          const float4* wr = reinterpret_cast<const float4*>(W_s + o * DP);
+          const float4* pr = reinterpret_cast<const float4*>(phi_s + u * DP);
+          float acc = 0.0f;
+          for (int i4 = 0; i4 < (D >> 2); i4++) {
+            const float4 a = wr[i4], b = pr[i4];
+            acc = __fmaf_rn(a.x, b.x, acc);
+            acc = __fmaf_rn(a.y, b.y, acc);
+            acc = __fmaf_rn(a.z, b.z, acc);
+            acc = __fmaf_rn(a.w, b.w, acc);
+          }
+          for (int i = D & ~3; i < D; i++) acc = __fmaf_rn(W_s[o * DP + i], phi_s[u * DP + i], acc);
+          mlp_s[u * OMAX + o] = acc;
+        }
+      }
+      if (need) {
+        cls_s[lane] = pc.cls;
+        wgt_s[lane] = fmul(conf, mag);
+      }
     }
-#pragma unroll
-    for (int o = 0; o < OMAX; o++) c_s[lane * OMAX + o] = cvec[o];
     mag_s[lane] = mag;
     __syncwarp();
 
@@ -126,9 +170,17 @@ __global__ void __launch_bounds__(kFeatWarps * 32, 4) features_kernel(Scene sc, 
         m &= m - 1;
         const float mg = mag_s[src];
         ogs = fadd(ogs, mg);
-        if (mg > 1e-7f) {
+        if (mg > 1e-7f) {  // a lane with features: conf > 0 and in this pixel
+          const float wg = wgt_s[src];
+          const float4* mr = reinterpret_cast<const float4*>(mlp_s + cls_s[src] * OMAX);
 #pragma unroll
-          for (int o = 0; o < OMAX; o++) acc[o] = fadd(acc[o], c_s[src * OMAX + o]);
+          for (int o4 = 0; o4 < OMAX / 4; o4++) {
+            const float4 x = mr[o4];
+            acc[4 * o4] = fadd(acc[4 * o4], fmul(x.x, wg));
+            acc[4 * o4 + 1] = fadd(acc[4 * o4 + 1], fmul(x.y, wg));
+            acc[4 * o4 + 2] = fadd(acc[4 * o4 + 2], fmul(x.z, wg));
+            acc[4 * o4 + 3] = fadd(acc[4 * o4 + 3], fmul(x.w, wg));
+          }
         }
       }
       if (!(ogs < 1e-7f)) {
@@ -164,7 +216,7 @@ __global__ void __launch_bounds__(kFeatWarps * 32, 4) features_kernel(Scene sc, 
 template <int F, int OMAX>
 void launch_features_t(const Scene& sc, GeomState& g, cudaStream_t s) {
   const int D = sc.L * F;
-  size_t smem = sizeof(float) * (D * OMAX + OMAX + sc.L + kFeatWarps * (32 * OMAX + 32));
+  size_t smem = sizeof(float) * (feat_head_floats(D, sc.L, OMAX) + kFeatWarps * feat_warp_floats(D, OMAX));
   auto k = features_kernel<F, OMAX>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   int blocks = (sc.P + kFeatWarps - 1) / kFeatWarps;

@@ -165,36 +165,79 @@ __device__ __forceinline__ float corner_weight(const LevelCorners& c, int k) {
   return ((k & 4) ? c.wx1 : c.wx0) * ((k & 2) ? c.wy1 : c.wy0) * ((k & 1) ? c.wz1 : c.wz0);
 }
 
-// Trilinear hashgrid features of one point, level by level (hashgrid.h:207-299).
-// For each level, fn(l, acc) receives the F interpolated features.  `on` lanes
-// gather; the warp walks the union of the lanes' active corners in ascending
-// order, so a warp of points clamped to one face of the hashgrid box makes one
-// pass per level instead of eight.  Must be called by the whole warp.
-template <int F, typename Fn>
-__device__ __forceinline__ void for_each_level(const Scene& sc, const float* resf, float3 pos, bool on, Fn&& fn) {
-  const uint32_t p0 = (uint32_t)__ldg(sc.primes), p1 = (uint32_t)__ldg(sc.primes + 1),
-                 p2 = (uint32_t)__ldg(sc.primes + 2);
-  const float3 nrm = hash_norm(pos);
-  for (int l = 0; l < sc.L; l++) {
-    const LevelCorners c = level_corners(nrm, __ldg(sc.res + l), resf[l], __ldg(sc.do_hash + l) != 0, p0, p1, p2, sc.T);
-    const uint32_t mine = on ? c.mask : 0u;
-    float acc[F];
+// Trilinear hashgrid features of one (position, level) query (hashgrid.h:244-287),
+// accumulated into acc[F].  Each lane may hold a different position and level:
+// the eight corners are unrolled, so the corner choice is resolved at compile
+// time and only the per-lane mask test remains.  Corners are visited in
+// ascending k with weight (wx * wy) * wz, as in the reference.
+template <int F, bool POW2>
+__device__ __forceinline__ void gather_level(const LevelCorners& c, const float* __restrict__ lvl, uint32_t stride,
+                                             uint32_t T, uint32_t Tmask, float* acc) {
+  const uint32_t hxy[4] = {c.hsh ? c.ix0 ^ c.iy0 : c.ix0 + c.iy0, c.hsh ? c.ix0 ^ c.iy1 : c.ix0 + c.iy1,
+                           c.hsh ? c.ix1 ^ c.iy0 : c.ix1 + c.iy0, c.hsh ? c.ix1 ^ c.iy1 : c.ix1 + c.iy1};
+  const float wxy[4] = {c.wx0 * c.wy0, c.wx0 * c.wy1, c.wx1 * c.wy0, c.wx1 * c.wy1};
 #pragma unroll
-    for (int f = 0; f < F; f++) acc[f] = 0.0f;
-    const float* lvl = sc.table + (size_t)l * F;
-    uint32_t um = __reduce_or_sync(0xffffffffu, mine);
-    while (um) {
-      const int k = __ffs(um) - 1;
-      um &= um - 1;
-      if ((mine >> k) & 1u) {
-        const float w = corner_weight(c, k);
-        const FVec<F> v = load_feat<F>(lvl + (size_t)corner_index(c, k, sc.T, sc.Tmask) * sc.L * F);
-#pragma unroll
-        for (int f = 0; f < F; f++) acc[f] += v.v[f] * w;
+  for (int k = 0; k < 8; k++) {
+    if ((c.mask >> k) & 1u) {
+      const uint32_t z = (k & 1) ? c.iz1 : c.iz0;
+      uint32_t e;
+      if (c.hsh) {
+        const uint32_t h = hxy[k >> 1] ^ z;
+        e = POW2 ? (h & Tmask) : (h % T);
+      } else {
+        e = hxy[k >> 1] + z;
       }
+      const float w = wxy[k >> 1] * ((k & 1) ? c.wz1 : c.wz0);
+      const FVec<F> v = load_feat<F>(lvl + (size_t)e * stride);
+#pragma unroll
+      for (int f = 0; f < F; f++) acc[f] += v.v[f] * w;
     }
-    fn(l, acc);
   }
 }
+
+// Lanes of a warp grouped by bit-identical normalised hashgrid position: every
+// member of a class reads the same table entries with the same weights, so the
+// class's features are gathered once.  Points clamped to a face of the fixed
+// hashgrid box share positions, which is why a primitive often has one or three
+// classes rather than one per grid point.  Must be called by the whole warp.
+struct PosClasses {
+  uint32_t leaders;  // lowest member lane of every class
+  uint32_t peers;    // members of this lane's class (member lanes only)
+  int U;             // number of classes
+  int cls;           // this lane's class index, 0..U-1 (member lanes only)
+};
+__device__ __forceinline__ PosClasses pos_classes(float3 nrm, bool member) {
+  const uint32_t full = 0xffffffffu, lane = threadIdx.x & 31u;
+  const uint32_t mm = __ballot_sync(full, member);
+  const uint32_t peers = __match_any_sync(full, __float_as_uint(nrm.x)) & __match_any_sync(full, __float_as_uint(nrm.y)) &
+                         __match_any_sync(full, __float_as_uint(nrm.z)) & mm;
+  PosClasses pc;
+  pc.peers = peers;
+  pc.leaders = __ballot_sync(full, member && (peers & ((1u << lane) - 1u)) == 0u);
+  pc.U = __popc(pc.leaders);
+  pc.cls = member ? __popc(pc.leaders & ((1u << (__ffs(peers) - 1)) - 1u)) : 0;
+  return pc;
+}
+
+// Walks the items (class u, level l), u-major, of a warp: lane i starts at item i
+// and advances by 32 items per step.
+struct ItemWalk {
+  int u, l, su, sl, L;
+  __device__ __forceinline__ explicit ItemWalk(int levels) : L(levels) {
+    const int lane = (int)(threadIdx.x & 31u);
+    u = lane / L;
+    l = lane - u * L;
+    su = 32 / L;
+    sl = 32 - su * L;
+  }
+  __device__ __forceinline__ void next() {
+    u += su;
+    l += sl;
+    if (l >= L) {
+      l -= L;
+      u++;
+    }
+  }
+};
 
 }  // namespace vi
