@@ -12,7 +12,8 @@
 //     projections put every grid point in the same pixel; otherwise the
 //     record is recomputed with the backward projection).
 //  2. backward_prim: one warp per primitive, lane = grid point, gathers its
-//     contributing records and produces
+//     contributing records and produces (hashgrid work once per distinct
+//     normalised position of the primitive's grid points)
 //       dconf[q,g]  = sum_p (dIn_p . phi_g) * g'_{p,g}                (backward.cu:697-710)
 //       dtable      += (sum_p dIn_p * g'_{p,g} * conf_g) * corner weight (hashgrid.h:43-95)
 //       dW, db      += dpre_p (x) in_p, dpre_p                          (backward.cu:621-641)
@@ -186,50 +187,107 @@ __device__ __forceinline__ void atomic_vec(float* p, const float* x) {
   }
 }
 
-constexpr int kBwdWarps = 8;
+constexpr int kBwdWarps = 4;
 
-// Floats of shared memory each warp of backward_prim_kernel owns: phi rows, E
-// rows and its dW partial sums.
-__host__ __device__ inline int bwd_warp_floats(int D, int OMAX) { return 32 * (D + 1) + 32 * OMAX + OMAX * D; }
+__host__ __device__ inline int pad4(int x) { return (x + 3) & ~3; }
+__host__ __device__ inline int bwd_dp(int D) { return pad4(D) + 4; }
+// Shared memory of backward_prim_kernel.  Head: W [OMAX][DP] (rows of the
+// linear layer), dW [OMAX][D] and db [OMAX] partial sums of the CTA, level
+// resolution / hash flag [L].  Per warp: phi [32][DP] (features of each position
+// class), two lane rows [32][OMAX] (conf * vA and E of each grid point; the first
+// later holds W phi of each class), two class rows [32][OMAX] (their sums per
+// class), class positions [32] float4 and class member masks [32].
+__host__ __device__ inline int bwd_head_floats(int D, int L, int OMAX) {
+  return OMAX * bwd_dp(D) + pad4(OMAX * D) + OMAX + 3 * pad4(L);
+}
+__host__ __device__ inline int bwd_warp_floats(int D, int OMAX) { return 32 * bwd_dp(D) + 4 * 32 * OMAX + 4 * 32 + 32; }
+
+// Gathers the features of one (position, level) query into acc[F] and, when doA,
+// scatters A[f] * (corner weight) into the table gradient at each corner
+// (hashgrid.h:43-95): the same corners, weights and order as gather_level.
+template <int F, bool POW2>
+__device__ __forceinline__ void gather_scatter_level(const LevelCorners& c, const float* __restrict__ lvl,
+                                                     float* __restrict__ dst, uint32_t stride, uint32_t T,
+                                                     uint32_t Tmask, bool doA, const float* A, float* acc) {
+  const uint32_t hxy[4] = {c.hsh ? c.ix0 ^ c.iy0 : c.ix0 + c.iy0, c.hsh ? c.ix0 ^ c.iy1 : c.ix0 + c.iy1,
+                           c.hsh ? c.ix1 ^ c.iy0 : c.ix1 + c.iy0, c.hsh ? c.ix1 ^ c.iy1 : c.ix1 + c.iy1};
+  const float wxy[4] = {c.wx0 * c.wy0, c.wx0 * c.wy1, c.wx1 * c.wy0, c.wx1 * c.wy1};
+#pragma unroll
+  for (int k = 0; k < 8; k++) {
+    if ((c.mask >> k) & 1u) {
+      const uint32_t z = (k & 1) ? c.iz1 : c.iz0;
+      uint32_t e;
+      if (c.hsh) {
+        const uint32_t h = hxy[k >> 1] ^ z;
+        e = POW2 ? (h & Tmask) : (h % T);
+      } else {
+        e = hxy[k >> 1] + z;
+      }
+      const float w = wxy[k >> 1] * ((k & 1) ? c.wz1 : c.wz0);
+      const FVec<F> v = load_feat<F>(lvl + (size_t)e * stride);
+#pragma unroll
+      for (int f = 0; f < F; f++) acc[f] += v.v[f] * w;
+      if (doA) {
+        float x[F];
+#pragma unroll
+        for (int f = 0; f < F; f++) x[f] = A[f] * w;
+        atomic_vec<F>(dst + (size_t)e * stride, x);
+      }
+    }
+  }
+}
 
 // One warp per primitive, lane g = grid point g.  With dIn_p = W^T dpre_p
 // (backward.cu:608-619), every per-pair sum collapses onto O-wide vectors:
 //   v_g  = sum_p g'_{p,g} dpre_p                 -> dconf_g = v_g . (W phi_g)
-//   vA_g = sum_p [|g' conf_g| > 1e-9] g' dpre_p  -> table coefficient conf_g W^T vA_g
+//   vA_g = sum_p [|g' conf_g| > 1e-9] g' dpre_p  -> table coefficient W^T (conf_g vA_g)
 //   E_g  = w_g dpre_{p(g)}                       -> dW += E_g (x) phi_g
-// so each contributing pixel costs O multiply-adds per lane, and the hashgrid
-// gather (for phi_g) and scatter (for the table gradient) share one level loop.
+// Grid points at the same normalised hashgrid position share phi and table
+// corners, so conf*vA and E are summed per position class; the hashgrid gather
+// (for phi) and scatter (for the table gradient) then run once per (class,
+// level), spread over the warp's lanes.
 template <int F, int OMAX>
-__global__ void __launch_bounds__(kBwdWarps * 32, 3) backward_prim_kernel(Scene sc, GeomState g, float* __restrict__ dconf,
+__global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene sc, GeomState g, float* __restrict__ dconf,
                                                                       float* __restrict__ dtable, float* __restrict__ dW,
                                                                       float* __restrict__ db) {
-  extern __shared__ float smem[];
-  const int L = sc.L, D = L * F, O = sc.O, V = sc.V, G = sc.G;
-  const int DS = D + 1;
-  float* W_s = smem;              // [D][OMAX]: W transposed
-  float* dW_s = W_s + D * OMAX;   // [OMAX][D]
-  float* db_s = dW_s + OMAX * D;  // [OMAX]
-  float* resf_s = db_s + OMAX;    // [L] level resolutions as float
+  extern __shared__ float4 smem4[];
+  float* smem = reinterpret_cast<float*>(smem4);
+  const int L = sc.L, D = L * F, DP = bwd_dp(D), O = sc.O, V = sc.V, G = sc.G;
+  float* W_s = smem;                                      // [OMAX][DP]
+  float* dW_s = W_s + OMAX * DP;                          // [OMAX][D]
+  float* db_s = dW_s + pad4(OMAX * D);                    // [OMAX]
+  float* resf_s = db_s + OMAX;                            // [L]
+  int* res_s = reinterpret_cast<int*>(resf_s + pad4(L));  // [L]
+  int* hash_s = res_s + pad4(L);                          // [L]
   const int w = threadIdx.x >> 5;
   const uint32_t lane = threadIdx.x & 31;
-  float* phi_s = resf_s + L + w * bwd_warp_floats(D, OMAX);  // [32][DS]
-  float* E_s = phi_s + 32 * DS;                                        // [32][OMAX]
-  float* dWw = E_s + 32 * OMAX;  // [OMAX][D] this warp's dW partial sums; lane j owns columns j, j+32
-  for (int i = (int)lane; i < OMAX * D; i += 32) dWw[i] = 0.0f;
+  float* phi_s = smem + bwd_head_floats(D, L, OMAX) + w * bwd_warp_floats(D, OMAX);  // [32][DP]
+  float* cv_s = phi_s + 32 * DP;      // [32][OMAX] lane conf*vA, then class W phi
+  float* el_s = cv_s + 32 * OMAX;     // [32][OMAX] lane E
+  float* S_s = el_s + 32 * OMAX;      // [32][OMAX] class sum of conf*vA
+  float* Es_s = S_s + 32 * OMAX;      // [32][OMAX] class sum of E
+  float4* npos_s = reinterpret_cast<float4*>(Es_s + 32 * OMAX);  // [32]
+  uint32_t* mem_s = reinterpret_cast<uint32_t*>(npos_s + 32);     // [32]
 
-  for (int i = threadIdx.x; i < D * OMAX; i += blockDim.x) {
-    const int d = i / OMAX, o = i % OMAX;
-    W_s[i] = o < O ? sc.Wl[o * D + d] : 0.0f;
-    dW_s[i] = 0.0f;
+  for (int i = threadIdx.x; i < OMAX * DP; i += blockDim.x) {
+    const int o = i / DP, d = i % DP;
+    W_s[i] = o < O && d < D ? sc.Wl[o * D + d] : 0.0f;
   }
+  for (int i = threadIdx.x; i < OMAX * D; i += blockDim.x) dW_s[i] = 0.0f;
   for (int i = threadIdx.x; i < OMAX; i += blockDim.x) db_s[i] = 0.0f;
-  for (int i = threadIdx.x; i < L; i += blockDim.x) resf_s[i] = (float)sc.res[i];
+  for (int i = threadIdx.x; i < L; i += blockDim.x) {
+    res_s[i] = sc.res[i];
+    resf_s[i] = (float)sc.res[i];
+    hash_s[i] = sc.do_hash[i];
+  }
   __syncthreads();
 
   const Stencil st = make_stencil(sc.genus);
   const GridPt gpt = grid_point((int)lane < V ? (int)lane : 0, G, sc.gof);
   const uint32_t p0 = (uint32_t)__ldg(sc.primes), p1 = (uint32_t)__ldg(sc.primes + 1),
                  p2 = (uint32_t)__ldg(sc.primes + 2);
+  const uint32_t lt_mask = (1u << lane) - 1u;
+  const uint32_t stride = (uint32_t)D;
   float dbacc = 0.0f;
 
   // Primitives are handed out in batches of kGrab per warp from a counter
@@ -284,7 +342,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) backward_prim_kernel(Scene 
       if (((inm >> lane) & 1u) && wE != 0.0f) {
         hasE = true;
 #pragma unroll
-        for (int o = 0; o < OMAX; o++) E_s[lane * OMAX + o] = fmul(wE, dpre[o]);
+        for (int o = 0; o < OMAX; o++) el_s[lane * OMAX + o] = fmul(wE, dpre[o]);
       }
       const float gp = act ? occ_mag(inm, gpt, G, st) : 0.0f;
       if (gp > 1e-7f) {
@@ -299,117 +357,120 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) backward_prim_kernel(Scene 
         }
       }
     }
-    if (!__any_sync(0xffffffffu, hasE || hasV)) continue;
-
-    // One pass over the levels: gather phi_g (for dconf and dW), scatter the table gradient.
-    float2 mlp2[OMAX / 2];
-#pragma unroll
-    for (int o = 0; o < OMAX / 2; o++) mlp2[o] = make_float2(0.0f, 0.0f);
-    float* phi_row = phi_s + lane * DS;
     const bool gather = hasE || hasV;
+    if (!__any_sync(0xffffffffu, gather)) continue;
+
+    // Lane rows, then position classes of the gathering lanes.
+    if (!hasE) {
+#pragma unroll
+      for (int o = 0; o < OMAX; o++) el_s[lane * OMAX + o] = 0.0f;
+    }
+#pragma unroll
+    for (int o = 0; o < OMAX; o++) cv_s[lane * OMAX + o] = hasA ? conf * vA[o] : 0.0f;
     const float3 nrm = hash_norm(pos);
+    const PosClasses pc = pos_classes(nrm, gather);
     const uint32_t amask = __ballot_sync(0xffffffffu, hasA);
-    const int afirst = amask ? __ffs(amask) - 1 : 0;
-#pragma unroll 1
-    for (int l = 0; l < L; l++) {
-      const LevelCorners lc =
-          level_corners(nrm, __ldg(sc.res + l), resf_s[l], __ldg(sc.do_hash + l) != 0, p0, p1, p2, sc.T);
-      const uint32_t cmask = (gather || hasA) ? lc.mask : 0u;
-      float acc[F], a[F];
-#pragma unroll
-      for (int f = 0; f < F; f++) {
-        acc[f] = 0.0f;
-        // table coefficient of this level: conf_g * sum_o W[o][l*F+f] vA[o]
-        float2 sum = make_float2(0.0f, 0.0f);
-        const float2* wr = reinterpret_cast<const float2*>(W_s + (l * F + f) * OMAX);
-#pragma unroll
-        for (int o = 0; o < OMAX / 2; o++) sum = __ffma2_rn(wr[o], make_float2(vA[2 * o], vA[2 * o + 1]), sum);
-        a[f] = conf * (sum.x + sum.y);
-      }
-      // Every lane with a table gradient on the same cell set (points clamped to
-      // the hashgrid box): sum per corner across the warp, one atomic per corner.
-      bool uni = false;
-      if (amask) {
-        const uint32_t m0 = __shfl_sync(0xffffffffu, cmask, afirst);
-        const uint32_t i0 = __shfl_sync(0xffffffffu, lc.ix0, afirst);
-        const uint32_t j0 = __shfl_sync(0xffffffffu, lc.iy0, afirst);
-        const uint32_t k0 = __shfl_sync(0xffffffffu, lc.iz0, afirst);
-        uni = __all_sync(0xffffffffu, !hasA || (cmask == m0 && lc.ix0 == i0 && lc.iy0 == j0 && lc.iz0 == k0)) &&
-              __popc(amask) > 1;
-      }
-      const float* lvl = sc.table + (size_t)l * F;
-      float* dst = dtable + (size_t)l * F;
-      uint32_t um = __reduce_or_sync(0xffffffffu, cmask);
-      while (um) {
-        const int k = __ffs(um) - 1;
-        um &= um - 1;
-        const bool on = (cmask >> k) & 1u;
-        const uint32_t e = on ? corner_index(lc, k, sc.T, sc.Tmask) : 0u;
-        const float cw = on ? corner_weight(lc, k) : 0.0f;
-        if (gather && on) {
-          const FVec<F> x = load_feat<F>(lvl + (size_t)e * L * F);
-#pragma unroll
-          for (int f = 0; f < F; f++) acc[f] += x.v[f] * cw;
+    const uint32_t emask = __ballot_sync(0xffffffffu, hasE);
+    if (gather && (pc.peers & lt_mask) == 0u) {
+      npos_s[pc.cls] = make_float4(nrm.x, nrm.y, nrm.z, 0.0f);
+      mem_s[pc.cls] = pc.peers;
+    }
+    __syncwarp();
+    // Class sums over (class, output) items, members in lane order.
+    for (int base = 0; base < pc.U * OMAX; base += 32) {
+      const int item = base + (int)lane, u = item / OMAX, o = item % OMAX;
+      if (u < pc.U) {
+        float sa = 0.0f, se = 0.0f;
+        uint32_t mm = mem_s[u];
+        while (mm) {
+          const int src = __ffs(mm) - 1;
+          mm &= mm - 1;
+          sa += cv_s[src * OMAX + o];
+          se += el_s[src * OMAX + o];
         }
-        if (uni) {
-          if ((__shfl_sync(0xffffffffu, cmask, afirst) >> k) & 1u) {
-            float x[F];
-#pragma unroll
-            for (int f = 0; f < F; f++) {
-              float y = hasA ? a[f] * cw : 0.0f;
-#pragma unroll
-              for (int off = 16; off > 0; off >>= 1) y += __shfl_xor_sync(0xffffffffu, y, off);
-              x[f] = y;
-            }
-            if ((int)lane == afirst) atomic_vec<F>(dst + (size_t)e * L * F, x);
-          }
-        } else if (hasA && on) {
-          float x[F];
-#pragma unroll
-          for (int f = 0; f < F; f++) x[f] = a[f] * cw;
-          atomic_vec<F>(dst + (size_t)e * L * F, x);
-        }
-      }
-#pragma unroll
-      for (int f = 0; f < F; f++) {
-        const float x = acc[f];
-        const float2* wr = reinterpret_cast<const float2*>(W_s + (l * F + f) * OMAX);
-#pragma unroll
-        for (int o = 0; o < OMAX / 2; o++) mlp2[o] = __ffma2_rn(wr[o], make_float2(x, x), mlp2[o]);
-        if (hasE) phi_row[l * F + f] = x;
+        S_s[u * OMAX + o] = sa;
+        Es_s[u * OMAX + o] = se;
       }
     }
+    __syncwarp();
+
+    // One pass over (class, level) items: gather phi, scatter the table gradient.
+    ItemWalk it(L);
+    for (int base = 0; base < pc.U * L; base += 32, it.next()) {
+      if (it.u < pc.U) {
+        const float4 n4 = npos_s[it.u];
+        const LevelCorners lc = level_corners(make_float3(n4.x, n4.y, n4.z), res_s[it.l], resf_s[it.l],
+                                              hash_s[it.l] != 0, p0, p1, p2, sc.T);
+        const bool doA = (mem_s[it.u] & amask) != 0u;
+        float A[F], acc[F];
+#pragma unroll
+        for (int f = 0; f < F; f++) {
+          acc[f] = 0.0f;
+          // table coefficient of this level: sum_o W[o][l*F+f] S_u[o]
+          float sum = 0.0f;
+          if (doA) {
+#pragma unroll
+            for (int o = 0; o < OMAX; o++) sum += W_s[o * DP + it.l * F + f] * S_s[it.u * OMAX + o];
+          }
+          A[f] = sum;
+        }
+        const float* lvl = sc.table + (size_t)it.l * F;
+        float* dst = dtable + (size_t)it.l * F;
+        if (sc.Tmask)
+          gather_scatter_level<F, true>(lc, lvl, dst, stride, sc.T, sc.Tmask, doA, A, acc);
+        else
+          gather_scatter_level<F, false>(lc, lvl, dst, stride, sc.T, sc.Tmask, doA, A, acc);
+#pragma unroll
+        for (int f = 0; f < F; f++) phi_s[it.u * DP + it.l * F + f] = acc[f];
+      }
+    }
+    __syncwarp();
+    // W phi per class (into cv_s, free now): i ascending.
+    float* mlp_s = cv_s;
+    for (int base = 0; base < pc.U * OMAX; base += 32) {
+      const int item = base + (int)lane, u = item / OMAX, o = item % OMAX;
+      if (u < pc.U) {
+        const float4* wr = reinterpret_cast<const float4*>(W_s + o * DP);
+        const float4* pr = reinterpret_cast<const float4*>(phi_s + u * DP);
+        float acc = 0.0f;
+        for (int i4 = 0; i4 < (D >> 2); i4++) {
+          const float4 a = wr[i4], b = pr[i4];
+          acc = __fmaf_rn(a.x, b.x, acc);
+          acc = __fmaf_rn(a.y, b.y, acc);
+          acc = __fmaf_rn(a.z, b.z, acc);
+          acc = __fmaf_rn(a.w, b.w, acc);
+        }
+        for (int i = D & ~3; i < D; i++) acc = __fmaf_rn(W_s[o * DP + i], phi_s[u * DP + i], acc);
+        mlp_s[u * OMAX + o] = acc;
+      }
+    }
+    __syncwarp();
     if (act) {
       float dX = 0.0f;
+      if (gather) {
+        const float* mr = mlp_s + pc.cls * OMAX;
 #pragma unroll
-      for (int o = 0; o < OMAX / 2; o++) dX += v[2 * o] * mlp2[o].x + v[2 * o + 1] * mlp2[o].y;
+        for (int o = 0; o < OMAX / 2; o++) dX += v[2 * o] * mr[2 * o] + v[2 * o + 1] * mr[2 * o + 1];
+      }
       dconf[s0 + lane] = dX;
     }
-    // dW += E_g (x) phi_g over the lanes with an E contribution.
-    const uint32_t em = __ballot_sync(0xffffffffu, hasE);
-    __syncwarp();
-    for (int jj = (int)lane; jj < D; jj += 32) {
-      float acc[OMAX];
+    // dW += (class sum of E) (x) phi_class, into the CTA's partial sums.
+    if (emask) {
+      for (int u = 0; u < pc.U; u++) {
+        if ((mem_s[u] & emask) == 0u) continue;
+        for (int jj = (int)lane; jj < D; jj += 32) {
+          const float x = phi_s[u * DP + jj];
 #pragma unroll
-      for (int o = 0; o < OMAX; o++) acc[o] = dWw[o * D + jj];
-      uint32_t mm = em;
-      while (mm) {
-        const int gg = __ffs(mm) - 1;
-        mm &= mm - 1;
-        const float x = phi_s[gg * DS + jj];
-#pragma unroll
-        for (int o = 0; o < OMAX; o++) acc[o] += E_s[gg * OMAX + o] * x;
+          for (int o = 0; o < OMAX; o++)
+            if (o < O) atomicAdd(&dW_s[o * D + jj], Es_s[u * OMAX + o] * x);
+        }
       }
-#pragma unroll
-      for (int o = 0; o < OMAX; o++) dWw[o * D + jj] = acc[o];
     }
     __syncwarp();
   }
 
-  // CTA reduction of dW and db, then one global atomic per element.
+  // CTA reduction of db, then one global atomic per element of dW and db.
   __syncwarp();
-  for (int i = (int)lane; i < O * D; i += 32)
-    if (dWw[i] != 0.0f) atomicAdd(&dW_s[i], dWw[i]);
   if ((int)lane < O && dbacc != 0.0f) atomicAdd(&db_s[lane], dbacc);
   __syncthreads();
   for (int i = threadIdx.x; i < O * D; i += blockDim.x)
@@ -421,12 +482,12 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) backward_prim_kernel(Scene 
 template <int F, int OMAX>
 void launch_prim_t(const Scene& sc, GeomState& g, float* dconf, float* dtable, float* dW, float* db, cudaStream_t s) {
   const int D = sc.L * F;
-  size_t smem = sizeof(float) * (2 * OMAX * D + OMAX + sc.L + kBwdWarps * bwd_warp_floats(D, OMAX));
+  size_t smem = sizeof(float) * (bwd_head_floats(D, sc.L, OMAX) + kBwdWarps * bwd_warp_floats(D, OMAX));
   auto k = backward_prim_kernel<F, OMAX>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   cudaMemsetAsync(g.status + 5, 0, sizeof(uint32_t), s);
   int blocks = (sc.P + kBwdWarps - 1) / kBwdWarps;
-  blocks = blocks < 148 * 8 ? blocks : 148 * 8;
+  blocks = blocks < 148 * 10 ? blocks : 148 * 10;
   if (blocks < 1) blocks = 1;
   k<<<blocks, kBwdWarps * 32, smem, s>>>(sc, g, dconf, dtable, dW, db);
   note_launches(1);
