@@ -320,6 +320,16 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
     const float mag = act ? occ_mag(posm, gpt, G, st) : 0.0f;
     const float wE = (act && conf > 0.0f && mag > 1e-7f) ? fmul(conf, mag) : 0.0f;
 
+    // dL/dpre of every contributing record, loaded in parallel (lane j: record j)
+    // and staged in S_s, which is free until the class sums.
+    if ((cm >> lane) & 1u) {
+      const float4* src = reinterpret_cast<const float4*>(g.rec_dpre + (s0 + lane) * OMAX);
+      float4* dstr = reinterpret_cast<float4*>(S_s + lane * OMAX);
+#pragma unroll
+      for (int o4 = 0; o4 < OMAX / 4; o4++) dstr[o4] = src[o4];
+    }
+    __syncwarp();
+
     float v[OMAX], vA[OMAX];
 #pragma unroll
     for (int o = 0; o < OMAX; o++) v[o] = vA[o] = 0.0f;
@@ -328,16 +338,15 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
     while (m) {
       const int j = __ffs(m) - 1;
       m &= m - 1;
-      const size_t slot = s0 + j;
       const int ppix = (int)__shfl_sync(0xffffffffu, rp, j) - 1;  // pixel of this contribution
       float dpre[OMAX];
-      const float4* src = reinterpret_cast<const float4*>(g.rec_dpre + slot * OMAX);
+      const float4* src = reinterpret_cast<const float4*>(S_s + j * OMAX);
 #pragma unroll
       for (int o4 = 0; o4 < OMAX / 4; o4++) {
         const float4 x = src[o4];
         dpre[4 * o4] = x.x; dpre[4 * o4 + 1] = x.y; dpre[4 * o4 + 2] = x.z; dpre[4 * o4 + 3] = x.w;
       }
-      if ((int)lane < O) dbacc += g.rec_dpre[slot * OMAX + lane];
+      if ((int)lane < O) dbacc += S_s[j * OMAX + lane];
       const uint32_t inm = __ballot_sync(0xffffffffu, bpix == ppix);
       if (((inm >> lane) & 1u) && wE != 0.0f) {
         hasE = true;
@@ -358,6 +367,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
       }
     }
     const bool gather = hasE || hasV;
+    __syncwarp();  // S_s reads done before the class sums overwrite it
     if (!__any_sync(0xffffffffu, gather)) continue;
 
     // Lane rows, then position classes of the gathering lanes.

@@ -14,7 +14,8 @@
 // passes the reference's 1e-7 test becomes one record:
 //   key   = tile * 256 + pixel-in-tile (only tiles inside the primitive's rect)
 //   props = sigmoid(acc + b) for colour and features, exp(acc + b) for density.
-// Records of a primitive are stored sorted by key in slots [q*V, q*V + count).
+// Records of a primitive are stored grouped by tile, ascending, in slots
+// [q*V, q*V + count).
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -192,13 +193,18 @@ __global__ void __launch_bounds__(kFeatWarps * 32, 4) features_kernel(Scene sc, 
         }
       }
     }
+    // Records are grouped by tile, ascending, and in lane order inside a tile
+    // (the render finds a tile's records by key; their order inside it is free).
     const uint32_t recmask = __ballot_sync(0xffffffffu, is_rec);
-    const uint32_t rkey = ((ty * sc.gx + tx) << 8) | (((unsigned)fy & 15u) << 4) | ((unsigned)fx & 15u);
-    uint32_t rank = 0;
-#pragma unroll 4
-    for (int l = 0; l < 32; l++) {
-      const uint32_t k = __shfl_sync(0xffffffffu, rkey, l);
-      if (((recmask >> l) & 1u) && k < rkey) rank++;
+    const uint32_t tkey = ty * sc.gx + tx;
+    const uint32_t rkey = (tkey << 8) | (((unsigned)fy & 15u) << 4) | ((unsigned)fx & 15u);
+    uint32_t rank = 0, rem = recmask;
+    while (rem) {
+      const uint32_t t = __shfl_sync(0xffffffffu, tkey, __ffs(rem) - 1);
+      const uint32_t grp = __ballot_sync(0xffffffffu, is_rec && tkey == t);
+      rem &= ~grp;
+      if (t < tkey) rank += __popc(grp);
+      else if (t == tkey) rank += __popc(grp & lt_mask);
     }
     if (is_rec) {
       const size_t slot = (size_t)q * V + rank;

@@ -124,9 +124,9 @@ __device__ __forceinline__ LevelCorners level_corners(float3 nrm, int res, float
   c.wz0 = 1.0f - t.z; c.wz1 = t.z;
   uint32_t mx = t.x != 0.0f ? 3u : 1u, my = t.y != 0.0f ? 3u : 1u, mz = t.z != 0.0f ? 3u : 1u;
   if (hsh) {
-    c.ix0 = (uint32_t)b.x * p0; c.ix1 = (uint32_t)(b.x + 1) * p0;
-    c.iy0 = (uint32_t)b.y * p1; c.iy1 = (uint32_t)(b.y + 1) * p1;
-    c.iz0 = (uint32_t)b.z * p2; c.iz1 = (uint32_t)(b.z + 1) * p2;
+    c.ix0 = (uint32_t)b.x * p0; c.ix1 = c.ix0 + p0;
+    c.iy0 = (uint32_t)b.y * p1; c.iy1 = c.iy0 + p1;
+    c.iz0 = (uint32_t)b.z * p2; c.iz1 = c.iz0 + p2;
   } else {
     // dense grid: index z*res^2 + y*res + x (uint32, as the reference), in range only
     const uint32_t r = (uint32_t)res;
@@ -140,7 +140,11 @@ __device__ __forceinline__ LevelCorners level_corners(float3 nrm, int res, float
   uint32_t m = ((mx & 1u) ? 0x0fu : 0u) | ((mx & 2u) ? 0xf0u : 0u);
   m &= ((my & 1u) ? 0x33u : 0u) | ((my & 2u) ? 0xccu : 0u);
   m &= ((mz & 1u) ? 0x55u : 0u) | ((mz & 2u) ? 0xaau : 0u);
-  if (!hsh) {
+  // Dense index bound: the corner sums grow with each offset, so when the
+  // highest corner in the mask is below T (and res^3 cannot wrap) all are.
+  const bool small = res < 1625;
+  const uint32_t top = ((m & 0xf0u) ? c.ix1 : c.ix0) + ((m & 0xccu) ? c.iy1 : c.iy0) + ((m & 0xaau) ? c.iz1 : c.iz0);
+  if (!hsh && !(small && top < T)) {
     uint32_t mm = m;
     while (mm) {
       const int k = __ffs(mm) - 1;
