@@ -192,15 +192,19 @@ constexpr int kBwdWarps = 4;
 __host__ __device__ inline int pad4(int x) { return (x + 3) & ~3; }
 __host__ __device__ inline int bwd_dp(int D) { return pad4(D) + 4; }
 // Shared memory of backward_prim_kernel.  Head: W [OMAX][DP] (rows of the
-// linear layer), dW [OMAX][D] and db [OMAX] partial sums of the CTA, level
-// resolution / hash flag [L].  Per warp: phi [32][DP] (features of each position
-// class), two lane rows [32][OMAX] (conf * vA and E of each grid point; the first
-// later holds W phi of each class), two class rows [32][OMAX] (their sums per
-// class), class positions [32] float4 and class member masks [32].
+// linear layer), db [OMAX] partial sums of the CTA, level resolution / hash
+// flag [L].  Per warp: phi [32][DP] (features of each position class), two lane
+// rows [32][OMAX] (conf * vA and E of each grid point; the first later holds W
+// phi of each class), two class rows [32][OMAX] (their sums per class; the first
+// stages the records' dL/dpre before that), class positions [32] float4, class
+// member masks [32] and the warp's dW partial sums [OMAX][D] (lane j owns
+// columns j, j + 32).
 __host__ __device__ inline int bwd_head_floats(int D, int L, int OMAX) {
-  return OMAX * bwd_dp(D) + pad4(OMAX * D) + OMAX + 3 * pad4(L);
+  return OMAX * bwd_dp(D) + OMAX + 3 * pad4(L);
 }
-__host__ __device__ inline int bwd_warp_floats(int D, int OMAX) { return 32 * bwd_dp(D) + 4 * 32 * OMAX + 4 * 32 + 32; }
+__host__ __device__ inline int bwd_warp_floats(int D, int OMAX) {
+  return 32 * bwd_dp(D) + 4 * 32 * OMAX + 4 * 32 + 32 + OMAX * D;
+}
 
 // Gathers the features of one (position, level) query into acc[F] and, when doA,
 // scatters A[f] * (corner weight) into the table gradient at each corner
@@ -254,8 +258,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
   float* smem = reinterpret_cast<float*>(smem4);
   const int L = sc.L, D = L * F, DP = bwd_dp(D), O = sc.O, V = sc.V, G = sc.G;
   float* W_s = smem;                                      // [OMAX][DP]
-  float* dW_s = W_s + OMAX * DP;                          // [OMAX][D]
-  float* db_s = dW_s + pad4(OMAX * D);                    // [OMAX]
+  float* db_s = W_s + OMAX * DP;                          // [OMAX]
   float* resf_s = db_s + OMAX;                            // [L]
   int* res_s = reinterpret_cast<int*>(resf_s + pad4(L));  // [L]
   int* hash_s = res_s + pad4(L);                          // [L]
@@ -268,12 +271,13 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
   float* Es_s = S_s + 32 * OMAX;      // [32][OMAX] class sum of E
   float4* npos_s = reinterpret_cast<float4*>(Es_s + 32 * OMAX);  // [32]
   uint32_t* mem_s = reinterpret_cast<uint32_t*>(npos_s + 32);     // [32]
+  float* dWw = reinterpret_cast<float*>(mem_s + 32);              // [OMAX][D]
 
   for (int i = threadIdx.x; i < OMAX * DP; i += blockDim.x) {
     const int o = i / DP, d = i % DP;
     W_s[i] = o < O && d < D ? sc.Wl[o * D + d] : 0.0f;
   }
-  for (int i = threadIdx.x; i < OMAX * D; i += blockDim.x) dW_s[i] = 0.0f;
+  for (int i = (int)(threadIdx.x & 31); i < OMAX * D; i += 32) dWw[i] = 0.0f;
   for (int i = threadIdx.x; i < OMAX; i += blockDim.x) db_s[i] = 0.0f;
   for (int i = threadIdx.x; i < L; i += blockDim.x) {
     res_s[i] = sc.res[i];
@@ -302,10 +306,10 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
     }
     const int q = q0 + qi++;
     if (q >= sc.P) break;
-    const uint32_t n = g.rec_cnt[q] & ~kBwdDiffers;
-    if (n == 0) continue;
     const size_t s0 = (size_t)q * V;
-    const uint32_t rp = lane < n ? g.rec_pix[s0 + lane] : 0u;
+    // rec_pix is zero except in slots of contributing records (the record count
+    // need not be read first).
+    const uint32_t rp = (int)lane < V ? g.rec_pix[s0 + lane] : 0u;
     const uint32_t cm = __ballot_sync(0xffffffffu, rp != 0u);
     if (cm == 0) continue;
 
@@ -334,36 +338,86 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
 #pragma unroll
     for (int o = 0; o < OMAX; o++) v[o] = vA[o] = 0.0f;
     bool hasE = false, hasV = false, hasA = false;
-    uint32_t m = cm;
-    while (m) {
-      const int j = __ffs(m) - 1;
-      m &= m - 1;
-      const int ppix = (int)__shfl_sync(0xffffffffu, rp, j) - 1;  // pixel of this contribution
-      float dpre[OMAX];
+    // g'_{p,g} dL/dpre_p summed over the contributing records p.
+    auto add_record = [&](int j, float gp) {
+      hasV = true;
+      const bool doA = fabsf(fmul(gp, conf)) > 1e-9f;
+      hasA |= doA;
       const float4* src = reinterpret_cast<const float4*>(S_s + j * OMAX);
 #pragma unroll
       for (int o4 = 0; o4 < OMAX / 4; o4++) {
-        const float4 x = src[o4];
-        dpre[4 * o4] = x.x; dpre[4 * o4 + 1] = x.y; dpre[4 * o4 + 2] = x.z; dpre[4 * o4 + 3] = x.w;
+        const float4 d = src[o4];
+        const float x0 = gp * d.x, x1 = gp * d.y, x2 = gp * d.z, x3 = gp * d.w;
+        v[4 * o4] += x0; v[4 * o4 + 1] += x1; v[4 * o4 + 2] += x2; v[4 * o4 + 3] += x3;
+        if (doA) {
+          vA[4 * o4] += x0; vA[4 * o4 + 1] += x1; vA[4 * o4 + 2] += x2; vA[4 * o4 + 3] += x3;
+        }
       }
-      if ((int)lane < O) dbacc += S_s[j * OMAX + lane];
-      const uint32_t inm = __ballot_sync(0xffffffffu, bpix == ppix);
-      if (((inm >> lane) & 1u) && wE != 0.0f) {
+    };
+    if (st.S == 3) {
+      // 3-tap stencil: an axis adds 1/2 to record p exactly when one of the two
+      // neighbours along it lies in p's pixel (backward.cu:654-689), so a grid
+      // point only meets the records of its neighbours' pixels.  myrec = the
+      // record of this grid point's own pixel, or -1.
+      int myrec = -1;
+      uint32_t m = cm;
+      while (m) {
+        const int j = __ffs(m) - 1;
+        m &= m - 1;
+        const int ppix = (int)__shfl_sync(0xffffffffu, rp, j) - 1;
+        if (bpix == ppix) myrec = j;
+        if ((int)lane < O) dbacc += S_s[j * OMAX + lane];
+      }
+      if (myrec >= 0 && wE != 0.0f) {
         hasE = true;
 #pragma unroll
-        for (int o = 0; o < OMAX; o++) el_s[lane * OMAX + o] = fmul(wE, dpre[o]);
+        for (int o = 0; o < OMAX; o++) el_s[lane * OMAX + o] = fmul(wE, S_s[myrec * OMAX + o]);
       }
-      const float gp = act ? occ_mag(inm, gpt, G, st) : 0.0f;
-      if (gp > 1e-7f) {
-        hasV = true;
-        const bool doA = fabsf(fmul(gp, conf)) > 1e-9f;
-        hasA |= doA;
+      const int GG = G * G, gi = (int)lane;
+      int c[6];
+      c[0] = __shfl_sync(0xffffffffu, myrec, (gi + 31) & 31);
+      c[1] = __shfl_sync(0xffffffffu, myrec, (gi + 1) & 31);
+      c[2] = __shfl_sync(0xffffffffu, myrec, (gi + 32 - G) & 31);
+      c[3] = __shfl_sync(0xffffffffu, myrec, (gi + G) & 31);
+      c[4] = __shfl_sync(0xffffffffu, myrec, (gi + 32 - GG) & 31);
+      c[5] = __shfl_sync(0xffffffffu, myrec, (gi + GG) & 31);
+      if (!act || gpt.x == 0) c[0] = -1;
+      if (!act || gpt.x + 1 >= G) c[1] = -1;
+      if (!act || gpt.y == 0) c[2] = -1;
+      if (!act || gpt.y + 1 >= G) c[3] = -1;
+      if (!act || gpt.z == 0) c[4] = -1;
+      if (!act || gpt.z + 1 >= G) c[5] = -1;
 #pragma unroll
-        for (int o = 0; o < OMAX; o++) {
-          const float x = gp * dpre[o];
-          v[o] += x;
-          if (doA) vA[o] += x;
+      for (int a = 0; a < 3; a++)
+        if (c[2 * a] == c[2 * a + 1]) c[2 * a] = c[2 * a + 1] = -1;
+#pragma unroll
+      for (int i = 0; i < 6; i++) {
+        if (c[i] >= 0) {
+          int cnt = 1;
+#pragma unroll
+          for (int k = i + 1; k < 6; k++)
+            if (c[k] == c[i]) {
+              cnt++;
+              c[k] = -1;
+            }
+          add_record(c[i], 0.5f * (float)cnt);
         }
+      }
+    } else {
+      uint32_t m = cm;
+      while (m) {
+        const int j = __ffs(m) - 1;
+        m &= m - 1;
+        const int ppix = (int)__shfl_sync(0xffffffffu, rp, j) - 1;  // pixel of this contribution
+        if ((int)lane < O) dbacc += S_s[j * OMAX + lane];
+        const uint32_t inm = __ballot_sync(0xffffffffu, bpix == ppix);
+        if (((inm >> lane) & 1u) && wE != 0.0f) {
+          hasE = true;
+#pragma unroll
+          for (int o = 0; o < OMAX; o++) el_s[lane * OMAX + o] = fmul(wE, S_s[j * OMAX + o]);
+        }
+        const float gp = act ? occ_mag(inm, gpt, G, st) : 0.0f;
+        if (gp > 1e-7f) add_record(j, gp);
       }
     }
     const bool gather = hasE || hasV;
@@ -386,20 +440,42 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
       mem_s[pc.cls] = pc.peers;
     }
     __syncwarp();
-    // Class sums over (class, output) items, members in lane order.
-    for (int base = 0; base < pc.U * OMAX; base += 32) {
-      const int item = base + (int)lane, u = item / OMAX, o = item % OMAX;
-      if (u < pc.U) {
-        float sa = 0.0f, se = 0.0f;
-        uint32_t mm = mem_s[u];
-        while (mm) {
-          const int src = __ffs(mm) - 1;
-          mm &= mm - 1;
-          sa += cv_s[src * OMAX + o];
-          se += el_s[src * OMAX + o];
+    // Class sums of conf*vA and E.  Rows of lanes outside every class are zero.
+    if (pc.U == 1) {
+      // One class: lanes cover (vector, output[, half]) and sum rows directly.
+      static_assert(OMAX == 8 || OMAX == 16, "OMAX is 8 or 16");
+      if constexpr (OMAX == 8) {
+        const int half = (int)lane & 1, o = ((int)lane >> 1) & 7, vec = (int)lane >> 4;
+        const float* rows = vec ? el_s : cv_s;
+        float x = 0.0f;
+#pragma unroll
+        for (int r = 0; r < 16; r++) x += rows[(2 * r + half) * OMAX + o];
+        x += __shfl_xor_sync(0xffffffffu, x, 1);
+        if (half == 0) (vec ? Es_s : S_s)[o] = x;
+      } else {
+        const int o = (int)lane & 15, vec = (int)lane >> 4;
+        const float* rows = vec ? el_s : cv_s;
+        float x = 0.0f;
+#pragma unroll 8
+        for (int r = 0; r < 32; r++) x += rows[r * OMAX + o];
+        (vec ? Es_s : S_s)[o] = x;
+      }
+    } else {
+      // (class, output) items; members in lane order.
+      for (int base = 0; base < pc.U * OMAX; base += 32) {
+        const int item = base + (int)lane, u = item / OMAX, o = item % OMAX;
+        if (u < pc.U) {
+          float sa = 0.0f, se = 0.0f;
+          uint32_t mm = mem_s[u];
+          while (mm) {
+            const int src = __ffs(mm) - 1;
+            mm &= mm - 1;
+            sa += cv_s[src * OMAX + o];
+            se += el_s[src * OMAX + o];
+          }
+          S_s[u * OMAX + o] = sa;
+          Es_s[u * OMAX + o] = se;
         }
-        S_s[u * OMAX + o] = sa;
-        Es_s[u * OMAX + o] = se;
       }
     }
     __syncwarp();
@@ -435,25 +511,9 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
       }
     }
     __syncwarp();
-    // W phi per class (into cv_s, free now): i ascending.
+    // W phi per class (into cv_s, free now).
     float* mlp_s = cv_s;
-    for (int base = 0; base < pc.U * OMAX; base += 32) {
-      const int item = base + (int)lane, u = item / OMAX, o = item % OMAX;
-      if (u < pc.U) {
-        const float4* wr = reinterpret_cast<const float4*>(W_s + o * DP);
-        const float4* pr = reinterpret_cast<const float4*>(phi_s + u * DP);
-        float acc = 0.0f;
-        for (int i4 = 0; i4 < (D >> 2); i4++) {
-          const float4 a = wr[i4], b = pr[i4];
-          acc = __fmaf_rn(a.x, b.x, acc);
-          acc = __fmaf_rn(a.y, b.y, acc);
-          acc = __fmaf_rn(a.z, b.z, acc);
-          acc = __fmaf_rn(a.w, b.w, acc);
-        }
-        for (int i = D & ~3; i < D; i++) acc = __fmaf_rn(W_s[o * DP + i], phi_s[u * DP + i], acc);
-        mlp_s[u * OMAX + o] = acc;
-      }
-    }
+    class_linear<OMAX>(W_s, phi_s, DP, D, pc.U, mlp_s);
     __syncwarp();
     if (act) {
       float dX = 0.0f;
@@ -464,27 +524,30 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
       }
       dconf[s0 + lane] = dX;
     }
-    // dW += (class sum of E) (x) phi_class, into the CTA's partial sums.
+    // dW += (class sum of E) (x) phi_class; lane jj owns columns jj, jj + 32.
     if (emask) {
       for (int u = 0; u < pc.U; u++) {
         if ((mem_s[u] & emask) == 0u) continue;
         for (int jj = (int)lane; jj < D; jj += 32) {
           const float x = phi_s[u * DP + jj];
 #pragma unroll
-          for (int o = 0; o < OMAX; o++)
-            if (o < O) atomicAdd(&dW_s[o * D + jj], Es_s[u * OMAX + o] * x);
+          for (int o = 0; o < OMAX; o++) dWw[o * D + jj] += Es_s[u * OMAX + o] * x;
         }
       }
     }
     __syncwarp();
   }
 
-  // CTA reduction of db, then one global atomic per element of dW and db.
+  // CTA reduction of dW and db, then one global atomic per element.
   __syncwarp();
   if ((int)lane < O && dbacc != 0.0f) atomicAdd(&db_s[lane], dbacc);
   __syncthreads();
-  for (int i = threadIdx.x; i < O * D; i += blockDim.x)
-    if (dW_s[i] != 0.0f) atomicAdd(&dW[i], dW_s[i]);
+  const float* warp0 = smem + bwd_head_floats(D, L, OMAX) + (bwd_warp_floats(D, OMAX) - OMAX * D);
+  for (int i = threadIdx.x; i < O * D; i += blockDim.x) {
+    float x = 0.0f;
+    for (int ww = 0; ww < kBwdWarps; ww++) x += warp0[(size_t)ww * bwd_warp_floats(D, OMAX) + i];
+    if (x != 0.0f) atomicAdd(&dW[i], x);
+  }
   for (int i = threadIdx.x; i < O; i += blockDim.x)
     if (db_s[i] != 0.0f) atomicAdd(&db[i], db_s[i]);
 }

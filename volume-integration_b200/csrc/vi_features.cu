@@ -131,24 +131,8 @@ __global__ void __launch_bounds__(kFeatWarps * 32, 4) features_kernel(Scene sc, 
         }
       }
       __syncwarp();
-      // Linear layer per class: mlp[u][o] = sum_i W[o][i] phi_u[i], i ascending.
-      for (int base = 0; base < pc.U * OMAX; base += 32) {
-        const int item = base + lane, u = item / OMAX, o = item % OMAX;
-        if (u < pc.U) {
-          const float4* wr = reinterpret_cast<const float4*>(W_s + o * DP);
-          const float4* pr = reinterpret_cast<const float4*>(phi_s + u * DP);
-          float acc = 0.0f;
-          for (int i4 = 0; i4 < (D >> 2); i4++) {
-            const float4 a = wr[i4], b = pr[i4];
-            acc = __fmaf_rn(a.x, b.x, acc);
-            acc = __fmaf_rn(a.y, b.y, acc);
-            acc = __fmaf_rn(a.z, b.z, acc);
-            acc = __fmaf_rn(a.w, b.w, acc);
-          }
-          for (int i = D & ~3; i < D; i++) acc = __fmaf_rn(W_s[o * DP + i], phi_s[u * DP + i], acc);
-          mlp_s[u * OMAX + o] = acc;
-        }
-      }
+      // Linear layer per class: mlp[u][o] = sum_i W[o][i] phi_u[i].
+      class_linear<OMAX>(W_s, phi_s, DP, D, pc.U, mlp_s);
       if (need) {
         cls_s[lane] = pc.cls;
         wgt_s[lane] = fmul(conf, mag);

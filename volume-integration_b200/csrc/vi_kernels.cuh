@@ -223,6 +223,40 @@ __device__ __forceinline__ PosClasses pos_classes(float3 nrm, bool member) {
   return pc;
 }
 
+// W phi per position class: mlp[u * OMAX + o] = sum_i W[o][i] phi_u[i] for
+// u < U, with W rows and phi rows DP floats apart (16-byte aligned, D used).
+// When there are few (class, output) items, two or four lanes split one sum
+// and combine with shuffles.  Must be called by the whole warp.
+template <int OMAX>
+__device__ __forceinline__ void class_linear(const float* W_s, const float* phi_s, int DP, int D, int U, float* mlp_s) {
+  const int lane = (int)(threadIdx.x & 31u);
+  const int items = U * OMAX;
+  const int sh = items <= 8 ? 2 : (items <= 16 ? 1 : 0);  // log2 lanes per item
+  const int P = 1 << sh, n4 = D >> 2, per = (n4 + P - 1) >> sh;
+  for (int base = 0; base < (items << sh); base += 32) {
+    const int t = base + lane, item = t >> sh, part = t & (P - 1);
+    const int u = item / OMAX, o = item % OMAX;
+    float acc = 0.0f;
+    if (u < U) {
+      const float4* wr = reinterpret_cast<const float4*>(W_s + o * DP);
+      const float4* pr = reinterpret_cast<const float4*>(phi_s + u * DP);
+      const int i1 = min(n4, (part + 1) * per);
+      for (int i4 = part * per; i4 < i1; i4++) {
+        const float4 a = wr[i4], b = pr[i4];
+        acc = __fmaf_rn(a.x, b.x, acc);
+        acc = __fmaf_rn(a.y, b.y, acc);
+        acc = __fmaf_rn(a.z, b.z, acc);
+        acc = __fmaf_rn(a.w, b.w, acc);
+      }
+      if (part == P - 1)
+        for (int i = D & ~3; i < D; i++) acc = __fmaf_rn(W_s[o * DP + i], phi_s[u * DP + i], acc);
+    }
+    if (sh >= 1) acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    if (sh >= 2) acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    if (u < U && part == 0) mlp_s[u * OMAX + o] = acc;
+  }
+}
+
 // Walks the items (class u, level l), u-major, of a warp: lane i starts at item i
 // and advances by 32 items per step.
 struct ItemWalk {
