@@ -22,9 +22,16 @@ import sys
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
-for _p in (os.path.join(ROOT, "volume-integration_b200"), os.path.join(ROOT, "oracle"), os.path.join(ROOT, "tests")):
-    if _p not in sys.path:
-        sys.path.insert(0, _p)
+_PKG = os.path.join(ROOT, "volume-integration_b200")
+if _PKG not in sys.path:
+    sys.path.insert(0, _PKG)
+
+
+def _oracle_path():
+    """The CPU restatement is imported only by the CPU baseline and the reference arm."""
+    p = os.path.join(ROOT, "oracle")
+    if p not in sys.path:
+        sys.path.insert(0, p)
 
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
@@ -36,13 +43,14 @@ STAGES = ["preprocess", "depth_sort", "offsets", "features", "binning", "render"
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="headline")
     ap.add_argument("--cpu-seconds", type=float, default=20.0, help="budget of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-aabb", action="store_true", help="skip the run with the hashgrid box at the scene bounds")
     return ap.parse_args()
 
 
@@ -57,15 +65,37 @@ def measured_peaks():
 # ---------------------------------------------------------------------------
 # workload
 # ---------------------------------------------------------------------------
+def settings_from(kw, cam, device, **extra):
+    import volume_integration as vi
+    d = {k: (v.to(device) if isinstance(v, torch.Tensor) else v) for k, v in list(kw.items()) + list(cam.items())}
+    d.update(extra)
+    return vi.IntegrationSettings(**d)
+
+
+def frame_stats(means, conf, s):
+    """Overlaps R, visible primitives and pixel contributions of one forward (state views of the C ABI)."""
+    from volume_integration import _C
+    G = s.grid_size
+    R, _, _, _, geom, binning, img = _C.integrate_primitives(
+        means.contiguous().float(), conf.reshape(means.shape[0], G ** 3).contiguous().float(), s.primitive_scale,
+        s.viewmatrix, s.projmatrix, s.cam_pos, s.tanfovx, s.tanfovy, s.image_height, s.image_width, s.near_plane,
+        s.max_distance, s.feature_table, s.resolution, s.do_hash, s.primes, s.feature_offset, s.linear_weights,
+        s.linear_bias, s.stencil_genus, s.grid_size, s.max_primitives_per_ray, s.occupancy_threshold, s.bg_color,
+        s.input_feature_dim, s.output_feature_dim, s.intermediate_feature_dim, s.hashgrid_levels,
+        s.num_output_channels, s.debug)
+    v = _C.state_views(geom, binning, img, means.shape[0], R, s.image_height, s.image_width,
+                       s.max_primitives_per_ray, G, s.output_feature_dim)
+    return {"R": int(R), "Pv": int((v["radii"] > 0).sum()), "Kt": int(v["n_contrib"].sum())}
+
+
 def workload(config, rank, world, device):
     import vi_workloads as wl
-    import vi_testlib as tl
     means, conf, kw, cams = wl.make(config)
     c = wl.CONFIGS[config]
     if world > 1 and len(cams) < world:
         cams = wl.orbit(world, c["dist"], c["width"], c["height"], c["fov"])
     cam = cams[rank % len(cams)]
-    s = tl.settings_from(kw, cam, device)
+    s = settings_from(kw, cam, device)
     gen = torch.Generator().manual_seed(77 + rank)
     dc = torch.randn(3, s.image_height, s.image_width, generator=gen).to(device)
     df = torch.randn(s.output_feature_dim, s.image_height, s.image_width, generator=gen).to(device)
@@ -97,12 +127,16 @@ def algorithmic_bytes(st, s, P):
 # clocks during the timed region
 # ---------------------------------------------------------------------------
 class Clocks:
+    """nvidia-smi samples every 50 ms from before the warm-up on; `start()` and
+    `stop()` bracket the timed region by host time (the region begins and ends
+    with a device synchronise), and only samples taken inside it are kept."""
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
 
     def __init__(self, device):
-        self.proc = None
+        import threading
+        self.proc, self.lines, self.t0 = None, [], None
         try:
             bus = torch.cuda.get_device_properties(device).pci_bus_id
             sel = ["--id=" + bus]
@@ -110,22 +144,37 @@ class Clocks:
             sel = ["-i", str(device)]
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits",
-                                          "-lms", "200"] + sel, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                                          "-lms", "50"] + sel, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
                                          text=True)
         except Exception:
             self.proc = None
+            return
+
+        def reader():
+            for line in self.proc.stdout:
+                self.lines.append((time.time(), line))
+        self.thread = threading.Thread(target=reader, daemon=True)
+        self.thread.start()
+
+    def start(self):
+        self.t0 = time.time()
 
     def stop(self):
         if self.proc is None:
             return None
+        t1 = time.time()
+        time.sleep(0.06)
         self.proc.terminate()
         try:
-            out, _ = self.proc.communicate(timeout=5)
+            self.proc.wait(timeout=5)
         except Exception:
             self.proc.kill()
-            out = ""
+        self.thread.join(timeout=5)
+        t0 = self.t0 if self.t0 is not None else 0.0
         rows = []
-        for line in out.strip().splitlines():
+        for t, line in self.lines:
+            if not (t0 <= t <= t1 + 0.05):
+                continue
             parts = [x.strip() for x in line.split(",")]
             if len(parts) != 7:
                 continue
@@ -168,19 +217,17 @@ def run_ours(args):
     bl = s.linear_bias.clone().requires_grad_(True)
     leaves = [confp, table, Wl, bl]
 
-    def step(m, c, t, w, b):
-        oc, of, vis = vi.integrate_primitives(m, c, t, w, b, s)
+    def step(m, c, t, w, b, settings=s):
+        oc, of, vis = vi.integrate_primitives(m, c, t, w, b, settings)
         grads = torch.autograd.grad([oc, of], [c, t, w, b], [dc, df])
         allreduce_gradients(grads)  # sum over ranks (no-op with one rank)
         return oc, of, vis, grads
 
     # workload statistics for the roofline (one forward, outside timing)
-    from vi_testlib import gpu_state
-    st = gpu_state(means, conf, s)
-    stats = {"R": int(st["num_rendered"]), "Pv": int((st["radii"] > 0).sum()), "Kt": int(st["n_contrib"].sum())}
-    del st
+    stats = frame_stats(means, conf, s)
 
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)  # > 126 MB L2
+    clocks = Clocks(device.index)
     for _ in range(args.warmup):
         step(means, *leaves)
     torch.cuda.synchronize()
@@ -190,10 +237,10 @@ def run_ours(args):
     _C.profile_read(True)
     _C.profile_enable(True)
     launches0 = _C.kernel_launches()
-    clocks = Clocks(device.index)
     times = []
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     torch.cuda.synchronize()
+    clocks.start()
     for i in range(args.steps):
         flush.zero_()
         ev[i][0].record()
@@ -246,6 +293,9 @@ def run_ours(args):
             "gpu_launches": int(launches), "gpu_launches_per_step": round(launches / args.steps, 2),
             "clocks": clk}
 
+    if not args.no_aabb:
+        line["scene_bounds"] = run_scene_bounds(args, step, means, leaves, s, flush, world, dist, device, _C)
+
     if not args.no_e2e:
         line["e2e"] = run_e2e(args, vi, means, conf, s, dc, df, world, dist if world > 1 else None, device)
 
@@ -256,6 +306,44 @@ def run_ours(args):
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args.config, args.cpu_seconds)
         print(json.dumps(line), flush=True)
+
+
+def run_scene_bounds(args, step, means, leaves, s, flush, world, dist, device, _C):
+    """The same step with the hashgrid box set to the scene's own bounds (an
+    extension field).  The reference's fixed [-1.3, 1.3]^3 box clamps most
+    positions of this scene to its faces, where grid points share table
+    entries; inside its own bounds every grid point of a primitive reads its own
+    cells, which is the harder case for the hashgrid kernels."""
+    import dataclasses
+    pad = float(s.primitive_scale)
+    lo = (means.min(0).values - pad).tolist()
+    hi = (means.max(0).values + pad).tolist()
+    sb = dataclasses.replace(s, hash_bounds=tuple(lo + hi))
+    steps = max(1, min(args.steps, 50))
+    for _ in range(max(3, args.warmup)):
+        step(means, *leaves, settings=sb)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    _C.profile_read(True)
+    _C.profile_enable(True)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for i in range(steps):
+        flush.zero_()
+        ev[i][0].record()
+        step(means, *leaves, settings=sb)
+        ev[i][1].record()
+    torch.cuda.synchronize()
+    _C.profile_enable(False)
+    prof = _C.profile_read(True)
+    total_ms = sum(a.elapsed_time(b) for a, b in ev)
+    if world > 1:
+        t = torch.tensor([total_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    return {"value": round(world * steps / (total_ms / 1000.0), 3), "unit": "frames/s", "steps": steps,
+            "ms_per_step": round(total_ms / steps, 4), "hash_bounds": [round(v, 4) for v in lo + hi],
+            "stage_ms_per_step": {k: round(v[0] / steps, 4) for k, v in prof.items()}}
 
 
 def run_e2e(args, vi, means, conf, s, dc, df, world, dist, device):
@@ -316,6 +404,7 @@ _CPU_SCENES = {}
 
 
 def cpu_scene(config):
+    _oracle_path()
     import oracle as orc
     import vi_workloads as wl
     if config in _CPU_SCENES:
@@ -340,6 +429,7 @@ def cpu_frame_sample(config, budget_s, threads):
     """Times the oracle on a bounded sample of one frame: the full preprocess and
     binning, then render + backward on every k-th tile, extrapolated to all
     tiles.  Returns (frames/s, description)."""
+    _oracle_path()
     import oracle as orc
     sc, dc, dfe = cpu_scene(config)
     t0 = time.perf_counter()

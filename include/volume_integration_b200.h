@@ -88,6 +88,40 @@ int vi_integrate_primitives_backward(
     unsigned output_feature_dim, unsigned hashgrid_levels, unsigned num_output_channels,
     uint64_t feature_table_size, int P, int num_rendered, int debug, void* stream);
 
+/*
+ * The two calls above with a hashgrid box other than the reference's fixed
+ * [-1.3, 1.3]^3 (reference: hashgrid.h:23-24, :125-126, :225-226).  No
+ * counterpart in the reference: scenes larger than that box clamp most
+ * positions to its faces, and this lets them use their own bounds.
+ * hash_bounds: host pointer to 6 floats {lo_x, lo_y, lo_z, hi_x, hi_y, hi_z}
+ * with lo < hi per axis, or NULL for the reference's box.  Positions normalise
+ * as clamp((p - lo) / (hi - lo), 0, 1).  The backward must get the bounds the
+ * forward got.
+ */
+int vi_integrate_primitives_ex(
+    vi_resize_fn geom_buffer, void* geom_user, vi_resize_fn binning_buffer, void* binning_user,
+    vi_resize_fn img_buffer, void* img_user, float* out_color, float* out_features, float* visibility_info,
+    int* num_rendered, int P, const float* means3D, const float* primitive_confidences, float primitive_scale,
+    const float* viewmatrix, const float* projmatrix, const float* cam_pos, float tan_fovx, float tan_fovy,
+    int image_height, int image_width, float near_plane, float max_distance, const float* feature_table,
+    uint64_t feature_table_numel, const int* resolution, const int* do_hash, const int* primes, int feature_offset,
+    const float* linear_weights, uint64_t linear_weights_numel, const float* linear_bias,
+    uint64_t linear_bias_numel, int stencil_genus, int grid_size, int max_primitives_per_ray,
+    float occupancy_threshold, const float* bg_color, unsigned input_feature_dim, unsigned output_feature_dim,
+    unsigned intermediate_feature_dim, unsigned hashgrid_levels, unsigned num_output_channels, int debug,
+    void* stream, const float* hash_bounds);
+int vi_integrate_primitives_backward_ex(
+    float* dL_dmeans3D, float* dL_dconfidences, float* dL_dfeature_table, float* dL_dlinear_weights,
+    float* dL_dlinear_bias, const float* dL_dout_color, const float* dL_dout_features, char* geom_buffer,
+    char* binning_buffer, char* img_buffer, const float* means3D, const float* primitive_confidences,
+    float primitive_scale, const float* viewmatrix, const float* projmatrix, const float* cam_pos, float tan_fovx,
+    float tan_fovy, int image_height, int image_width, float near_plane, float max_distance,
+    const float* feature_table, const int* resolution, const int* do_hash, const int* primes, int feature_offset,
+    const float* linear_weights, const float* linear_bias, int stencil_genus, int grid_size,
+    int max_primitives_per_ray, float occupancy_threshold, const float* bg_color, unsigned input_feature_dim,
+    unsigned output_feature_dim, unsigned hashgrid_levels, unsigned num_output_channels,
+    uint64_t feature_table_size, int P, int num_rendered, int debug, void* stream, const float* hash_bounds);
+
 /* Frustum test per primitive (view-space z > 0.2).  Replaces markVisible
  * (reference: integrate_primitives.h:136-139, integrate_primitives.cu:436-462). */
 int vi_mark_visible(int P, const float* means3D, const float* viewmatrix, const float* projmatrix, uint8_t* present,

@@ -45,6 +45,7 @@ class Params(ctypes.Structure):
         ("bg", ctypes.c_void_p),
         ("F", ctypes.c_int), ("Fout", ctypes.c_int), ("L", ctypes.c_int),
         ("table_size", ctypes.c_uint64),
+        ("hlo", ctypes.c_float * 3), ("hext", ctypes.c_float * 3),
     ]
 
 
@@ -87,7 +88,7 @@ class Scene:
                  tanfovx, tanfovy, image_height, image_width, near_plane, max_distance,
                  feature_table, resolution, do_hash, primes, feature_offset,
                  linear_weights, linear_bias, stencil_genus, grid_size, max_primitives_per_ray,
-                 bg_color, input_feature_dim, output_feature_dim, hashgrid_levels):
+                 bg_color, input_feature_dim, output_feature_dim, hashgrid_levels, hash_bounds=None):
         self.means = _c(means3D, np.float32).reshape(-1, 3)
         self.P = self.means.shape[0]
         self.G = int(grid_size)
@@ -108,6 +109,13 @@ class Scene:
         self.genus, self.K = int(stencil_genus), int(max_primitives_per_ray)
         self.bg = _c(bg_color, np.float32).reshape(-1)
         self.F, self.Fout, self.L = int(input_feature_dim), int(output_feature_dim), int(hashgrid_levels)
+        # hashgrid box (lo, extent) per axis; the reference's is fixed (hashgrid.h:23-24)
+        if hash_bounds is None:
+            self.hlo, self.hext = [np.float32(-1.3)] * 3, [np.float32(2.6)] * 3
+        else:
+            hb = np.asarray(hash_bounds, np.float32).reshape(6)
+            self.hlo = [hb[a] for a in range(3)]
+            self.hext = [np.float32(hb[3 + a] - hb[a]) for a in range(3)]
 
     @staticmethod
     def from_settings(means3D, confidences, settings):
@@ -120,7 +128,7 @@ class Scene:
                      n(s.feature_table), n(s.resolution), n(s.do_hash), n(s.primes), s.feature_offset,
                      n(s.linear_weights), n(s.linear_bias), s.stencil_genus, s.grid_size,
                      s.max_primitives_per_ray, n(s.bg_color), s.input_feature_dim,
-                     s.output_feature_dim, s.hashgrid_levels)
+                     s.output_feature_dim, s.hashgrid_levels, getattr(s, "hash_bounds", None))
 
     @property
     def tiles(self):
@@ -141,6 +149,8 @@ class Scene:
         p.bg = _p(self.bg)
         p.F, p.Fout, p.L = self.F, self.Fout, self.L
         p.table_size = self.table.size
+        for a in range(3):
+            p.hlo[a], p.hext[a] = float(self.hlo[a]), float(self.hext[a])
         return p
 
 

@@ -240,6 +240,7 @@ typedef struct {
     const float *bg;
     int F, Fout, L;
     uint64_t table_size; /* feature_table.numel(), backward bound check hashgrid.h:88 */
+    float hlo[3], hext[3]; /* hashgrid box: lower corner, extent; the reference fixes -1.3, 2.6 (hashgrid.h:23-24) */
 } vio_params;
 
 /* Table entry index of one corner, or -1 (hashgrid.h:258-275 / :57-74). */
@@ -258,8 +259,9 @@ static int64_t corner_entry(int cx, int cy, int cz, int res, int use_hash, const
 }
 
 /* Level setup common to interpolation and gradient (hashgrid.h:225-242). */
-static void level_setup(f3 pos, int res, int *base, float *t) {
-    float n[3] = {(pos.x - -1.3f) / 2.6f, (pos.y - -1.3f) / 2.6f, (pos.z - -1.3f) / 2.6f};
+static void level_setup(const vio_params *p, f3 pos, int res, int *base, float *t) {
+    float n[3] = {(pos.x - p->hlo[0]) / p->hext[0], (pos.y - p->hlo[1]) / p->hext[1],
+                  (pos.z - p->hlo[2]) / p->hext[2]};
     for (int a = 0; a < 3; a++) {
         float v = fmaxf(0.0f, fminf(1.0f, n[a]));
         float pl = v * (float)res;
@@ -273,7 +275,7 @@ static void level_setup(f3 pos, int res, int *base, float *t) {
 static void hash_interp(const vio_params *p, f3 pos, int l, float *phi) {
     int res = p->res[l], b[3];
     float t[3];
-    level_setup(pos, res, b, t);
+    level_setup(p, pos, res, b, t);
     for (int f = 0; f < p->F; f++) {
         float acc = 0.0f;
         for (int dx = 0; dx < 2; dx++) {
@@ -296,7 +298,7 @@ static void hash_interp(const vio_params *p, f3 pos, int l, float *phi) {
 static void hash_grad(const vio_params *p, f3 pos, int l, const float *dphi, float *dtable, int threaded) {
     int res = p->res[l], b[3];
     float t[3];
-    level_setup(pos, res, b, t);
+    level_setup(p, pos, res, b, t);
     for (int dz = 0; dz < 2; dz++)
         for (int dy = 0; dy < 2; dy++)
             for (int dx = 0; dx < 2; dx++) {

@@ -5,10 +5,12 @@ import ctypes
 import os
 import re
 
+import numpy as np
 import pytest
 import torch
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+PKG = os.path.join(ROOT, "volume-integration_b200")
 HEADER = os.path.join(ROOT, "include", "volume_integration_b200.h")
 LIB = os.path.join(ROOT, "volume-integration_b200", "volume_integration", "libvi_b200.so")
 
@@ -72,3 +74,35 @@ def test_cam_pos_must_be_cuda():
     with pytest.raises(TypeError):
         vi.integrate_primitives(torch.zeros(2, 3), torch.zeros(2, 27), torch.zeros(1), torch.zeros(1),
                                 torch.zeros(1), s)
+
+
+def test_oracle_reference_box_is_the_default():
+    """The oracle with the reference's hashgrid box given explicitly is bit-identical to the default."""
+    import dataclasses
+    import vi_testlib as tl
+    means, conf, s = tl.custom_scene(P=60, W=32, H=24, seed=4, device="cpu")
+    _, a = tl.oracle_run(means, conf, s)
+    _, b = tl.oracle_run(means, conf, dataclasses.replace(s, hash_bounds=(-1.3, -1.3, -1.3, 1.3, 1.3, 1.3)))
+    for k in ("out_color", "out_features", "visibility"):
+        np.testing.assert_array_equal(a[k], b[k])
+    _, c = tl.oracle_run(means, conf, dataclasses.replace(s, hash_bounds=(-1.0, -1.0, -1.0, 1.0, 1.0, 1.0)))
+    assert not np.array_equal(a["out_color"], c["out_color"])
+
+
+def test_binding_raises_runtime_error_on_a_c_abi_error():
+    """A status code from the C ABI becomes a RuntimeError carrying vi_last_error()
+    (run in a child process: a binding built against a mismatched C++ runtime
+    crashes here instead of raising)."""
+    import subprocess
+    import sys
+    code = ("import sys; sys.path.insert(0, %r)\n"
+            "import torch\n"
+            "from volume_integration import _C\n"
+            "e = torch.empty(0, dtype=torch.uint8)\n"
+            "try:\n"
+            "    _C.state_views(e, e, e, -5, 0, 16, 16, 8, 3, 4)\n"
+            "except RuntimeError as ex:\n"
+            "    print('raised:', ex)\n") % PKG
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert "raised: volume_integration: bad layout query (status 1)" in r.stdout

@@ -147,3 +147,51 @@ def test_sort_pairs_matches_stable_argsort(n, begin, end):
     order = np.argsort(digit, kind="stable")
     np.testing.assert_array_equal(vs.cpu().numpy(), vals.numpy()[order])
     np.testing.assert_array_equal(ks.cpu().numpy().view(np.uint64), k[order])
+
+
+# Hashgrid box other than the reference's fixed [-1.3, 1.3]^3 (an extension):
+# parity with the oracle under the same box, and the reference box given
+# explicitly must reproduce the default call bit for bit.
+HASH_BOUNDS = {
+    "inside": dict(extent=1.0, bounds=(-1.1, -1.2, -1.0, 1.05, 1.15, 0.9)),
+    # big overlapping primitives: table values of the benchmark scenes keep the
+    # densities (and with them the transmittance cut-offs) away from saturation
+    "scene_aabb": dict(extent=3.0, scale=0.4, dist=8.0, table_range=1e-4, bounds=None),
+    "anisotropic": dict(extent=1.0, bounds=(-0.5, -2.0, -1.0, 0.5, 2.0, 3.0)),
+}
+
+
+@pytest.mark.parametrize("name", sorted(HASH_BOUNDS))
+def test_hash_bounds(name):
+    import dataclasses
+    cfg = dict(HASH_BOUNDS[name])
+    bounds = cfg.pop("bounds")
+    means, conf, s = tl.custom_scene(seed=zlib.crc32(name.encode()) % 1000, **cfg)
+    if bounds is None:  # the scene's own box, padded by half a primitive
+        lo = (means.min(0).values - s.primitive_scale).tolist()
+        hi = (means.max(0).values + s.primitive_scale).tolist()
+        bounds = tuple(lo + hi)
+    s = dataclasses.replace(s, hash_bounds=bounds)
+    g, o = _check(means, conf, s, seed=5)
+    assert g["num_rendered"] > 0
+
+
+def test_hash_bounds_reference_box_is_the_default():
+    import dataclasses
+    means, conf, s = tl.custom_scene(seed=11, extent=2.0)
+    dc, df = tl.random_grads(s, seed=2)
+    a = tl.run_gpu(means, conf, s, dc, df, state=False)
+    b = tl.run_gpu(means, conf, dataclasses.replace(s, hash_bounds=(-1.3, -1.3, -1.3, 1.3, 1.3, 1.3)), dc, df,
+                   state=False)
+    for k in ("out_color", "out_features", "visibility"):
+        np.testing.assert_array_equal(a[k], b[k])
+    tl.assert_grads(a["grads"], b["grads"])  # atomic summation order differs between calls
+
+
+def test_hash_bounds_rejects_an_empty_box():
+    import dataclasses
+    import volume_integration as vi
+    means, conf, s = tl.custom_scene(seed=12)
+    s = dataclasses.replace(s, hash_bounds=(0.0, 0.0, 0.0, 1.0, -1.0, 1.0))
+    with pytest.raises(RuntimeError, match="hash_bounds"):
+        vi.integrate_primitives(means, conf, s.feature_table, s.linear_weights, s.linear_bias, s)

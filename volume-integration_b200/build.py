@@ -25,7 +25,20 @@ LIB = os.path.join(PKG, "libvi_b200.so")
 SOURCES = ["vi_sort.cu", "vi_binning.cu", "vi_features.cu", "vi_render.cu", "vi_backward.cu", "vi_api.cu",
            "vi_sort_noalloc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-I" + INCLUDE]
+
+
+def _host_compilers():
+    """The distribution's gcc/g++, the toolchain torch's own C++ runtime matches.
+    A wrapper that points g++ at another GCC's support files (crt objects, libgcc)
+    builds an extension whose C++ exceptions crash while they are formatted, so
+    the system compilers are preferred when they exist."""
+    cc, cxx = "/usr/bin/gcc", "/usr/bin/g++"
+    return (cc, cxx) if os.path.exists(cc) and os.path.exists(cxx) else (None, None)
+
+
+_CC, _CXX = _host_compilers()
+NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-I" + INCLUDE] + \
+    (["-ccbin", _CXX] if _CXX else [])
 
 
 def _nvcc():
@@ -71,7 +84,7 @@ def build_lib(force=False, jobs=6):
             for f in [ex.submit(_compile, s, o) for s, o in work]:
                 f.result()
     if force or work or _stale(LIB, objs):
-        cmd = [_nvcc()] + ARCH + ["-shared", "-o", LIB] + objs
+        cmd = [_nvcc()] + ARCH + (["-ccbin", _CXX] if _CXX else []) + ["-shared", "-o", LIB] + objs
         subprocess.run(cmd, check=True)
     return LIB
 
@@ -100,6 +113,8 @@ setup(name="volume_integration_b200_ext",
       script_args=["-q", "build_ext", "--inplace", "--build-temp", "_build/ext"])
 """ % INCLUDE
     env = dict(os.environ)
+    if _CXX:
+        env["CC"], env["CXX"] = _CC, _CXX
     env.setdefault("MAX_JOBS", "4")
     env["TORCH_CUDA_ARCH_LIST"] = "10.0a"
     r = subprocess.run([sys.executable, "-c", script], cwd=HERE, capture_output=True, text=True, env=env)

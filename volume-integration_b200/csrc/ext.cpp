@@ -9,6 +9,7 @@
 #include <torch/extension.h>
 
 #include <tuple>
+#include <vector>
 
 #include "volume_integration_b200.h"
 
@@ -38,7 +39,15 @@ Tensor cuda_i32(const Tensor& t, const char* name) {
 }
 void ok(int rc) { TORCH_CHECK(rc == VI_OK, "volume_integration: ", vi_last_error(), " (status ", rc, ")"); }
 
-std::tuple<int, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor> integrate_primitives(
+// Hashgrid box {lo_x, lo_y, lo_z, hi_x, hi_y, hi_z}; empty = the reference's fixed box.
+const float* bounds_ptr(const std::vector<double>& hb, float* buf) {
+  if (hb.empty()) return nullptr;
+  TORCH_CHECK(hb.size() == 6, "hash_bounds needs 6 values (lo xyz, hi xyz), got ", hb.size());
+  for (int i = 0; i < 6; i++) buf[i] = (float)hb[i];
+  return buf;
+}
+
+std::tuple<int, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor> integrate_primitives_ex(
     const Tensor& means3D, const Tensor& primitive_confidences, const double primitive_scale,
     const Tensor& viewmatrix, const Tensor& projmatrix, const Tensor& cam_pos, const double tan_fovx,
     const double tan_fovy, const int64_t image_height, const int64_t image_width, const double near_plane,
@@ -47,8 +56,9 @@ std::tuple<int, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor> integrate_primit
     const int64_t stencil_genus, const int64_t grid_size, const int64_t max_primitives_per_ray,
     const double occupancy_threshold, const Tensor& bg_color, const int64_t input_feature_dim,
     const int64_t output_feature_dim, const int64_t intermediate_feature_dim, const int64_t hashgrid_levels,
-    const int64_t num_output_channels, const bool debug) {
+    const int64_t num_output_channels, const bool debug, const std::vector<double>& hash_bounds) {
   TORCH_CHECK(means3D.dim() == 2 && means3D.size(1) == 3, "means3D must have shape (P, 3)");
+  float hb[6];
   const at::cuda::CUDAGuard guard(means3D.device());
   const int P = (int)means3D.size(0), H = (int)image_height, W = (int)image_width;
   Tensor m = cuda_f32(means3D, "means3D"), c = cuda_f32(primitive_confidences, "primitive_confidences");
@@ -68,7 +78,7 @@ std::tuple<int, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor> integrate_primit
   auto bo = fo.dtype(torch::kUInt8);
   Tensor geom = torch::empty({0}, bo), binning = torch::empty({0}, bo), img = torch::empty({0}, bo);
   int num_rendered = 0;
-  ok(vi_integrate_primitives(
+  ok(vi_integrate_primitives_ex(
       resize_cb, &geom, resize_cb, &binning, resize_cb, &img, out_color.data_ptr<float>(),
       out_features.data_ptr<float>(), visibility.data_ptr<float>(), &num_rendered, P, m.data_ptr<float>(),
       c.data_ptr<float>(), (float)primitive_scale, vm.data_ptr<float>(), pm.data_ptr<float>(), cp.data_ptr<float>(),
@@ -78,11 +88,30 @@ std::tuple<int, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor> integrate_primit
       (int)grid_size, (int)max_primitives_per_ray, (float)occupancy_threshold, bg.data_ptr<float>(),
       (unsigned)input_feature_dim, (unsigned)output_feature_dim, (unsigned)intermediate_feature_dim,
       (unsigned)hashgrid_levels, (unsigned)num_output_channels, debug ? 1 : 0,
-      at::cuda::getCurrentCUDAStream().stream()));
+      at::cuda::getCurrentCUDAStream().stream(), bounds_ptr(hash_bounds, hb)));
   return {num_rendered, out_color, out_features, visibility, geom, binning, img};
 }
 
-std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> integrate_primitives_backward(
+// The reference's 30-argument signature (integrate_primitives.h:42-62).
+std::tuple<int, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor> integrate_primitives(
+    const Tensor& means3D, const Tensor& primitive_confidences, const double primitive_scale,
+    const Tensor& viewmatrix, const Tensor& projmatrix, const Tensor& cam_pos, const double tan_fovx,
+    const double tan_fovy, const int64_t image_height, const int64_t image_width, const double near_plane,
+    const double max_distance, const Tensor& feature_table, const Tensor& resolution, const Tensor& do_hash,
+    const Tensor& primes, const int64_t feature_offset, const Tensor& linear_weights, const Tensor& linear_bias,
+    const int64_t stencil_genus, const int64_t grid_size, const int64_t max_primitives_per_ray,
+    const double occupancy_threshold, const Tensor& bg_color, const int64_t input_feature_dim,
+    const int64_t output_feature_dim, const int64_t intermediate_feature_dim, const int64_t hashgrid_levels,
+    const int64_t num_output_channels, const bool debug) {
+  return integrate_primitives_ex(means3D, primitive_confidences, primitive_scale, viewmatrix, projmatrix, cam_pos,
+                                 tan_fovx, tan_fovy, image_height, image_width, near_plane, max_distance,
+                                 feature_table, resolution, do_hash, primes, feature_offset, linear_weights,
+                                 linear_bias, stencil_genus, grid_size, max_primitives_per_ray, occupancy_threshold,
+                                 bg_color, input_feature_dim, output_feature_dim, intermediate_feature_dim,
+                                 hashgrid_levels, num_output_channels, debug, {});
+}
+
+std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> integrate_primitives_backward_ex(
     const Tensor& dL_dout_color, const Tensor& dL_dout_features, const Tensor& geomBuffer,
     const Tensor& binningBuffer, const Tensor& imgBuffer, const Tensor& means3D, const Tensor& primitive_confidences,
     const double primitive_scale, const Tensor& viewmatrix, const Tensor& projmatrix, const Tensor& cam_pos,
@@ -93,8 +122,9 @@ std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> integrate_primitives_backward
     const int64_t max_primitives_per_ray, const double occupancy_threshold, const Tensor& bg_color,
     const int64_t input_feature_dim, const int64_t output_feature_dim, const int64_t hashgrid_levels,
     const int64_t num_output_channels, const int64_t feature_table_size, const int64_t P, const int64_t num_rendered,
-    const bool debug) {
+    const bool debug, const std::vector<double>& hash_bounds) {
   const at::cuda::CUDAGuard guard(means3D.device());
+  float hb[6];
   Tensor m = cuda_f32(means3D, "means3D"), c = cuda_f32(primitive_confidences, "primitive_confidences");
   Tensor vm = cuda_f32(viewmatrix, "viewmatrix"), pm = cuda_f32(projmatrix, "projmatrix");
   Tensor cp = cuda_f32(cam_pos, "cam_pos"), ft = aligned_table(feature_table);
@@ -110,7 +140,7 @@ std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> integrate_primitives_backward
   TORCH_CHECK(c.numel() == P * grid_size * grid_size * grid_size, "primitive_confidences must be (P, G^3)");
   Tensor dmeans = torch::empty_like(m), dconf = torch::empty_like(c), dtable = torch::empty_like(ft);
   Tensor dW = torch::empty_like(lw), db = torch::empty_like(lb);
-  ok(vi_integrate_primitives_backward(
+  ok(vi_integrate_primitives_backward_ex(
       dmeans.data_ptr<float>(), dconf.data_ptr<float>(), dtable.data_ptr<float>(), dW.data_ptr<float>(),
       db.data_ptr<float>(), gc.data_ptr<float>(), gf.numel() ? gf.data_ptr<float>() : nullptr,
       geomBuffer.numel() ? reinterpret_cast<char*>(geomBuffer.data_ptr()) : nullptr,
@@ -122,8 +152,29 @@ std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> integrate_primitives_backward
       lw.data_ptr<float>(), lb.data_ptr<float>(), (int)stencil_genus, (int)grid_size, (int)max_primitives_per_ray,
       (float)occupancy_threshold, bg.data_ptr<float>(), (unsigned)input_feature_dim, (unsigned)output_feature_dim,
       (unsigned)hashgrid_levels, (unsigned)num_output_channels, (uint64_t)feature_table_size, (int)P,
-      (int)num_rendered, debug ? 1 : 0, at::cuda::getCurrentCUDAStream().stream()));
+      (int)num_rendered, debug ? 1 : 0, at::cuda::getCurrentCUDAStream().stream(), bounds_ptr(hash_bounds, hb)));
   return {dmeans, dconf, dtable, dW, db};
+}
+
+// The reference's 37-argument signature (integrate_primitives.h:66-113).
+std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> integrate_primitives_backward(
+    const Tensor& dL_dout_color, const Tensor& dL_dout_features, const Tensor& geomBuffer,
+    const Tensor& binningBuffer, const Tensor& imgBuffer, const Tensor& means3D, const Tensor& primitive_confidences,
+    const double primitive_scale, const Tensor& viewmatrix, const Tensor& projmatrix, const Tensor& cam_pos,
+    const double tan_fovx, const double tan_fovy, const int64_t image_height, const int64_t image_width,
+    const double near_plane, const double max_distance, const Tensor& feature_table, const Tensor& resolution,
+    const Tensor& do_hash, const Tensor& primes, const int64_t feature_offset, const Tensor& linear_weights,
+    const Tensor& linear_bias, const int64_t stencil_genus, const int64_t grid_size,
+    const int64_t max_primitives_per_ray, const double occupancy_threshold, const Tensor& bg_color,
+    const int64_t input_feature_dim, const int64_t output_feature_dim, const int64_t hashgrid_levels,
+    const int64_t num_output_channels, const int64_t feature_table_size, const int64_t P, const int64_t num_rendered,
+    const bool debug) {
+  return integrate_primitives_backward_ex(
+      dL_dout_color, dL_dout_features, geomBuffer, binningBuffer, imgBuffer, means3D, primitive_confidences,
+      primitive_scale, viewmatrix, projmatrix, cam_pos, tan_fovx, tan_fovy, image_height, image_width, near_plane,
+      max_distance, feature_table, resolution, do_hash, primes, feature_offset, linear_weights, linear_bias,
+      stencil_genus, grid_size, max_primitives_per_ray, occupancy_threshold, bg_color, input_feature_dim,
+      output_feature_dim, hashgrid_levels, num_output_channels, feature_table_size, P, num_rendered, debug, {});
 }
 
 Tensor mark_visible(Tensor& means3D, Tensor& viewmatrix, Tensor& projmatrix) {
@@ -195,6 +246,10 @@ std::tuple<Tensor, Tensor> sort_pairs(const Tensor& keys, const Tensor& vals, in
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("integrate_primitives", &integrate_primitives, "Integrate Primitives CUDA forward");
   m.def("integrate_primitives_backward", &integrate_primitives_backward, "Integrate Primitives CUDA backward");
+  m.def("integrate_primitives_ex", &integrate_primitives_ex,
+        "integrate_primitives with a hashgrid box (31st argument: 6 floats, or [] for the reference's box)");
+  m.def("integrate_primitives_backward_ex", &integrate_primitives_backward_ex,
+        "integrate_primitives_backward with a hashgrid box (38th argument)");
   m.def("mark_visible", &mark_visible, "Mark Visible Primitives CUDA");
   m.def("state_views", &state_views, "Integer state of a forward call in the reference's formats");
   m.def("sort_pairs", &sort_pairs, "Stable radix sort of (uint64 key, uint32 value) pairs");

@@ -9,6 +9,7 @@
 #include <vector>
 #include <cstdint>
 #include <cstdio>
+#include <cmath>
 #include <cstring>
 
 #include "../../include/volume_integration_b200.h"
@@ -175,7 +176,7 @@ int make_scene(Scene& sc, int P, const float* means3D, const float* conf, float 
                const float* proj, float tanfovx, float tanfovy, int H, int W, float near_plane, float max_distance,
                const float* table, const int* res, const int* do_hash, const int* primes, int T, const float* Wl,
                const float* bl, int genus, int G, int K, const float* bg, unsigned F, unsigned Fout, unsigned L,
-               unsigned channels) {
+               unsigned channels, const float* hash_bounds) {
   if (channels != 3)
     return fail(VI_ERR_UNSUPPORTED, "num_output_channels=%u: only 3 colour channels are implemented (as the "
                                     "reference, forward.cu:838)", channels);
@@ -205,6 +206,18 @@ int make_scene(Scene& sc, int P, const float* means3D, const float* conf, float 
   sc.res = res; sc.do_hash = do_hash; sc.primes = primes; sc.Wl = Wl; sc.bl = bl; sc.bg = bg;
   sc.gx = (unsigned)(W + VI_TILE - 1) / VI_TILE;
   sc.gy = (unsigned)(H + VI_TILE - 1) / VI_TILE;
+  for (int a = 0; a < 3; a++) {
+    if (!hash_bounds) {
+      sc.hlo[a] = -1.3f;  // hashgrid.h:225-226
+      sc.hext[a] = 2.6f;
+      continue;
+    }
+    const float lo = hash_bounds[a], hi = hash_bounds[3 + a];
+    if (!(std::isfinite(lo) && std::isfinite(hi) && hi > lo) || !std::isfinite(hi - lo))
+      return fail(VI_ERR_INVALID_ARGUMENT, "hash_bounds axis %d: need finite lo < hi, got [%g, %g]", a, lo, hi);
+    sc.hlo[a] = lo;
+    sc.hext[a] = hi - lo;
+  }
   return VI_OK;
 }
 
@@ -236,7 +249,8 @@ extern "C" const char* vi_last_error(void) { return g_err; }
 
 extern "C" int vi_sort_end_bit(uint32_t num_tiles) { return 32 + tile_bits(num_tiles); }
 
-extern "C" int vi_integrate_primitives(
+namespace {
+int forward_impl(
     vi_resize_fn geom_buffer, void* geom_user, vi_resize_fn binning_buffer, void* binning_user,
     vi_resize_fn img_buffer, void* img_user, float* out_color, float* out_features, float* visibility_info,
     int* num_rendered, int P, const float* means3D, const float* primitive_confidences, float primitive_scale,
@@ -247,7 +261,7 @@ extern "C" int vi_integrate_primitives(
     uint64_t linear_bias_numel, int stencil_genus, int grid_size, int max_primitives_per_ray,
     float occupancy_threshold, const float* bg_color, unsigned input_feature_dim, unsigned output_feature_dim,
     unsigned intermediate_feature_dim, unsigned hashgrid_levels, unsigned num_output_channels, int debug,
-    void* stream) {
+    void* stream, const float* hash_bounds) {
   (void)cam_pos;
   (void)occupancy_threshold;  // has no effect in the reference either (forward.cu:118-140 is never called)
   cudaStream_t s = (cudaStream_t)stream;
@@ -259,7 +273,7 @@ extern "C" int vi_integrate_primitives(
                       tan_fovy, image_height, image_width, near_plane, max_distance, feature_table, resolution,
                       do_hash, primes, feature_offset, linear_weights, linear_bias, stencil_genus, grid_size,
                       max_primitives_per_ray, bg_color, input_feature_dim, output_feature_dim, hashgrid_levels,
-                      num_output_channels);
+                      num_output_channels, hash_bounds);
   if (rc) return rc;
   if (intermediate_feature_dim != hashgrid_levels * input_feature_dim)
     return fail(VI_ERR_INVALID_ARGUMENT,
@@ -359,7 +373,7 @@ extern "C" int vi_integrate_primitives(
   return VI_OK;
 }
 
-extern "C" int vi_integrate_primitives_backward(
+int backward_impl(
     float* dL_dmeans3D, float* dL_dconfidences, float* dL_dfeature_table, float* dL_dlinear_weights,
     float* dL_dlinear_bias, const float* dL_dout_color, const float* dL_dout_features, char* geom_buffer,
     char* binning_buffer, char* img_buffer, const float* means3D, const float* primitive_confidences,
@@ -369,7 +383,7 @@ extern "C" int vi_integrate_primitives_backward(
     const float* linear_weights, const float* linear_bias, int stencil_genus, int grid_size,
     int max_primitives_per_ray, float occupancy_threshold, const float* bg_color, unsigned input_feature_dim,
     unsigned output_feature_dim, unsigned hashgrid_levels, unsigned num_output_channels,
-    uint64_t feature_table_size, int P, int num_rendered, int debug, void* stream) {
+    uint64_t feature_table_size, int P, int num_rendered, int debug, void* stream, const float* hash_bounds) {
   (void)cam_pos;
   (void)occupancy_threshold;
   (void)binning_buffer;  // the backward walks per-pixel contributor lists, not tile lists
@@ -379,7 +393,7 @@ extern "C" int vi_integrate_primitives_backward(
                       tan_fovy, image_height, image_width, near_plane, max_distance, feature_table, resolution,
                       do_hash, primes, feature_offset, linear_weights, linear_bias, stencil_genus, grid_size,
                       max_primitives_per_ray, bg_color, input_feature_dim, output_feature_dim, hashgrid_levels,
-                      num_output_channels);
+                      num_output_channels, hash_bounds);
   if (rc) return rc;
   if (feature_table_size < (uint64_t)sc.T * sc.L * sc.F)
     return fail(VI_ERR_INVALID_ARGUMENT, "feature_table_size=%llu < feature_offset*L*F", (unsigned long long)feature_table_size);
@@ -404,6 +418,90 @@ extern "C" int vi_integrate_primitives_backward(
   launch_backward(sc, g, im, dL_dout_color, sc.Fout ? dL_dout_features : nullptr, dL_dconfidences,
                   dL_dfeature_table, dL_dlinear_weights, dL_dlinear_bias, s);
   return check(s, debug, "backward", g.status);
+}
+
+}  // namespace
+
+extern "C" int vi_integrate_primitives(
+    vi_resize_fn geom_buffer, void* geom_user, vi_resize_fn binning_buffer, void* binning_user,
+    vi_resize_fn img_buffer, void* img_user, float* out_color, float* out_features, float* visibility_info,
+    int* num_rendered, int P, const float* means3D, const float* primitive_confidences, float primitive_scale,
+    const float* viewmatrix, const float* projmatrix, const float* cam_pos, float tan_fovx, float tan_fovy,
+    int image_height, int image_width, float near_plane, float max_distance, const float* feature_table,
+    uint64_t feature_table_numel, const int* resolution, const int* do_hash, const int* primes, int feature_offset,
+    const float* linear_weights, uint64_t linear_weights_numel, const float* linear_bias,
+    uint64_t linear_bias_numel, int stencil_genus, int grid_size, int max_primitives_per_ray,
+    float occupancy_threshold, const float* bg_color, unsigned input_feature_dim, unsigned output_feature_dim,
+    unsigned intermediate_feature_dim, unsigned hashgrid_levels, unsigned num_output_channels, int debug,
+    void* stream) {
+  return forward_impl(geom_buffer, geom_user, binning_buffer, binning_user, img_buffer, img_user, out_color, out_features,
+                      visibility_info, num_rendered, P, means3D, primitive_confidences, primitive_scale, viewmatrix,
+                      projmatrix, cam_pos, tan_fovx, tan_fovy, image_height, image_width, near_plane, max_distance,
+                      feature_table, feature_table_numel, resolution, do_hash, primes, feature_offset, linear_weights,
+                      linear_weights_numel, linear_bias, linear_bias_numel, stencil_genus, grid_size,
+                      max_primitives_per_ray, occupancy_threshold, bg_color, input_feature_dim, output_feature_dim,
+                      intermediate_feature_dim, hashgrid_levels, num_output_channels, debug, stream, nullptr);
+}
+
+extern "C" int vi_integrate_primitives_ex(
+    vi_resize_fn geom_buffer, void* geom_user, vi_resize_fn binning_buffer, void* binning_user,
+    vi_resize_fn img_buffer, void* img_user, float* out_color, float* out_features, float* visibility_info,
+    int* num_rendered, int P, const float* means3D, const float* primitive_confidences, float primitive_scale,
+    const float* viewmatrix, const float* projmatrix, const float* cam_pos, float tan_fovx, float tan_fovy,
+    int image_height, int image_width, float near_plane, float max_distance, const float* feature_table,
+    uint64_t feature_table_numel, const int* resolution, const int* do_hash, const int* primes, int feature_offset,
+    const float* linear_weights, uint64_t linear_weights_numel, const float* linear_bias,
+    uint64_t linear_bias_numel, int stencil_genus, int grid_size, int max_primitives_per_ray,
+    float occupancy_threshold, const float* bg_color, unsigned input_feature_dim, unsigned output_feature_dim,
+    unsigned intermediate_feature_dim, unsigned hashgrid_levels, unsigned num_output_channels, int debug,
+    void* stream, const float* hash_bounds) {
+  return forward_impl(geom_buffer, geom_user, binning_buffer, binning_user, img_buffer, img_user, out_color, out_features,
+                      visibility_info, num_rendered, P, means3D, primitive_confidences, primitive_scale, viewmatrix,
+                      projmatrix, cam_pos, tan_fovx, tan_fovy, image_height, image_width, near_plane, max_distance,
+                      feature_table, feature_table_numel, resolution, do_hash, primes, feature_offset, linear_weights,
+                      linear_weights_numel, linear_bias, linear_bias_numel, stencil_genus, grid_size,
+                      max_primitives_per_ray, occupancy_threshold, bg_color, input_feature_dim, output_feature_dim,
+                      intermediate_feature_dim, hashgrid_levels, num_output_channels, debug, stream, hash_bounds);
+}
+
+extern "C" int vi_integrate_primitives_backward(
+    float* dL_dmeans3D, float* dL_dconfidences, float* dL_dfeature_table, float* dL_dlinear_weights,
+    float* dL_dlinear_bias, const float* dL_dout_color, const float* dL_dout_features, char* geom_buffer,
+    char* binning_buffer, char* img_buffer, const float* means3D, const float* primitive_confidences,
+    float primitive_scale, const float* viewmatrix, const float* projmatrix, const float* cam_pos, float tan_fovx,
+    float tan_fovy, int image_height, int image_width, float near_plane, float max_distance,
+    const float* feature_table, const int* resolution, const int* do_hash, const int* primes, int feature_offset,
+    const float* linear_weights, const float* linear_bias, int stencil_genus, int grid_size,
+    int max_primitives_per_ray, float occupancy_threshold, const float* bg_color, unsigned input_feature_dim,
+    unsigned output_feature_dim, unsigned hashgrid_levels, unsigned num_output_channels,
+    uint64_t feature_table_size, int P, int num_rendered, int debug, void* stream) {
+  return backward_impl(dL_dmeans3D, dL_dconfidences, dL_dfeature_table, dL_dlinear_weights, dL_dlinear_bias,
+                       dL_dout_color, dL_dout_features, geom_buffer, binning_buffer, img_buffer, means3D,
+                       primitive_confidences, primitive_scale, viewmatrix, projmatrix, cam_pos, tan_fovx, tan_fovy,
+                       image_height, image_width, near_plane, max_distance, feature_table, resolution, do_hash,
+                       primes, feature_offset, linear_weights, linear_bias, stencil_genus, grid_size,
+                       max_primitives_per_ray, occupancy_threshold, bg_color, input_feature_dim, output_feature_dim,
+                       hashgrid_levels, num_output_channels, feature_table_size, P, num_rendered, debug, stream, nullptr);
+}
+
+extern "C" int vi_integrate_primitives_backward_ex(
+    float* dL_dmeans3D, float* dL_dconfidences, float* dL_dfeature_table, float* dL_dlinear_weights,
+    float* dL_dlinear_bias, const float* dL_dout_color, const float* dL_dout_features, char* geom_buffer,
+    char* binning_buffer, char* img_buffer, const float* means3D, const float* primitive_confidences,
+    float primitive_scale, const float* viewmatrix, const float* projmatrix, const float* cam_pos, float tan_fovx,
+    float tan_fovy, int image_height, int image_width, float near_plane, float max_distance,
+    const float* feature_table, const int* resolution, const int* do_hash, const int* primes, int feature_offset,
+    const float* linear_weights, const float* linear_bias, int stencil_genus, int grid_size,
+    int max_primitives_per_ray, float occupancy_threshold, const float* bg_color, unsigned input_feature_dim,
+    unsigned output_feature_dim, unsigned hashgrid_levels, unsigned num_output_channels,
+    uint64_t feature_table_size, int P, int num_rendered, int debug, void* stream, const float* hash_bounds) {
+  return backward_impl(dL_dmeans3D, dL_dconfidences, dL_dfeature_table, dL_dlinear_weights, dL_dlinear_bias,
+                       dL_dout_color, dL_dout_features, geom_buffer, binning_buffer, img_buffer, means3D,
+                       primitive_confidences, primitive_scale, viewmatrix, projmatrix, cam_pos, tan_fovx, tan_fovy,
+                       image_height, image_width, near_plane, max_distance, feature_table, resolution, do_hash,
+                       primes, feature_offset, linear_weights, linear_bias, stencil_genus, grid_size,
+                       max_primitives_per_ray, occupancy_threshold, bg_color, input_feature_dim, output_feature_dim,
+                       hashgrid_levels, num_output_channels, feature_table_size, P, num_rendered, debug, stream, hash_bounds);
 }
 
 extern "C" int vi_mark_visible(int P, const float* means3D, const float* viewmatrix, const float* projmatrix,

@@ -39,7 +39,7 @@ __device__ void gather_generic(const Scene& sc, float3 pos, float* phi) {
     const bool hsh = sc.do_hash[l] != 0;
     int3 b;
     float3 t;
-    level_setup(pos, res, b, t);
+    level_setup(pos, sc.hlo, sc.hext, res, b, t);
     for (int f = 0; f < sc.F; f++) phi[l * sc.F + f] = 0.0f;
     for (int dx = 0; dx < 2; dx++) {
       float wx = dx == 0 ? 1.0f - t.x : t.x;
@@ -431,7 +431,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
     }
 #pragma unroll
     for (int o = 0; o < OMAX; o++) cv_s[lane * OMAX + o] = hasA ? conf * vA[o] : 0.0f;
-    const float3 nrm = hash_norm(pos);
+    const float3 nrm = hash_norm(pos, sc.hlo, sc.hext);
     const PosClasses pc = pos_classes(nrm, gather);
     const uint32_t amask = __ballot_sync(0xffffffffu, hasA);
     const uint32_t emask = __ballot_sync(0xffffffffu, hasE);

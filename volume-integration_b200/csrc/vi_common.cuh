@@ -84,13 +84,14 @@ __device__ __forceinline__ float3 grid_pos(float3 c, int g, int G, float step, f
   return p;
 }
 
-// Position normalised to the fixed scene box [-1.3, 1.3]^3 and clamped to [0, 1]
+// Position normalised to the hashgrid box and clamped to [0, 1]: (p - lo) / ext
+// per axis, where the reference's box is fixed at lo = -1.3, ext = 2.6
 // (hashgrid.h:225-235).  It does not depend on the level, so callers compute it
 // once per point.
-__device__ __forceinline__ float3 hash_norm(float3 pos) {
-  return make_float3(fmaxf(0.0f, fminf(1.0f, __fdiv_rn(fsub(pos.x, -1.3f), 2.6f))),
-                     fmaxf(0.0f, fminf(1.0f, __fdiv_rn(fsub(pos.y, -1.3f), 2.6f))),
-                     fmaxf(0.0f, fminf(1.0f, __fdiv_rn(fsub(pos.z, -1.3f), 2.6f))));
+__device__ __forceinline__ float3 hash_norm(float3 pos, const float* lo, const float* ext) {
+  return make_float3(fmaxf(0.0f, fminf(1.0f, __fdiv_rn(fsub(pos.x, lo[0]), ext[0]))),
+                     fmaxf(0.0f, fminf(1.0f, __fdiv_rn(fsub(pos.y, lo[1]), ext[1]))),
+                     fmaxf(0.0f, fminf(1.0f, __fdiv_rn(fsub(pos.z, lo[2]), ext[2]))));
 }
 
 // floor of x for 0 <= x < 2^23 on the FMA and integer pipes: adding 2^23 with
@@ -117,8 +118,8 @@ __device__ __forceinline__ void level_setup_n(float3 n, int res, int3& b, float3
   level_setup_nf(n, (float)res, b, t);
 }
 
-__device__ __forceinline__ void level_setup(float3 pos, int res, int3& b, float3& t) {
-  float3 n = hash_norm(pos);
+__device__ __forceinline__ void level_setup(float3 pos, const float* lo, const float* ext, int res, int3& b, float3& t) {
+  float3 n = hash_norm(pos, lo, ext);
   float rf = (float)res;
   float px = fmul(n.x, rf), py = fmul(n.y, rf), pz = fmul(n.z, rf);
   float fx = floorf(px), fy = floorf(py), fz = floorf(pz);

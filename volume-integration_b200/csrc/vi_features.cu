@@ -106,9 +106,9 @@ __global__ void __launch_bounds__(kFeatWarps * 32, 4) features_kernel(Scene sc, 
 
     if (__any_sync(0xffffffffu, need)) {
       // Features of each distinct position: items (class u, level l) over the lanes.
-      const PosClasses pc = pos_classes(hash_norm(pos), need);
+      const PosClasses pc = pos_classes(hash_norm(pos, sc.hlo, sc.hext), need);
       if (need && (pc.peers & lt_mask) == 0) {
-        const float3 n = hash_norm(pos);
+        const float3 n = hash_norm(pos, sc.hlo, sc.hext);
         npos_s[pc.cls] = make_float4(n.x, n.y, n.z, 0.0f);
       }
       __syncwarp();

@@ -110,6 +110,7 @@ struct Scene {
   const float* bg;
   uint64_t table_numel;
   unsigned gx, gy;
+  float hlo[3], hext[3];  // hashgrid box: lower corner and extent per axis (reference: -1.3, 2.6)
 };
 
 void launch_preprocess(const Scene& sc, GeomState& g, cudaStream_t s);

@@ -7,6 +7,7 @@ same ``VolumeIntegrator`` module (``:346-389``).  All work runs in the compiled
 extension ``_C`` over ``libvi_b200.so``; importing fails loudly if it is absent.
 """
 from dataclasses import dataclass, field
+from typing import Optional, Sequence
 
 import torch
 import torch.nn as nn
@@ -58,6 +59,10 @@ class IntegrationSettings:
     hashgrid_levels: int = 16
     num_output_channels: int = 3
     debug: bool = False
+    # Extension (no counterpart in the reference, which fixes the hashgrid box
+    # at [-1.3, 1.3]^3, hashgrid.h:23-24): (lo_x, lo_y, lo_z, hi_x, hi_y, hi_z)
+    # of the box positions are normalised to, or None for the reference's box.
+    hash_bounds: Optional[Sequence[float]] = None
 
 
 def _flat_confidences(conf, P, G):
@@ -73,6 +78,17 @@ def _flat_confidences(conf, P, G):
             f"Confidence grid flat dimension mismatch: expected {G ** 3}, got {conf.shape[1]}"
         return conf, None
     raise ValueError(f"primitive_confidences has unexpected shape: {conf.shape}")
+
+
+def _hash_bounds(s):
+    """The settings' hashgrid box as 6 floats, or None for the reference's fixed box."""
+    hb = getattr(s, "hash_bounds", None)
+    if hb is None:
+        return None
+    vals = [float(v) for v in (hb.flatten().tolist() if isinstance(hb, torch.Tensor) else hb)]
+    if len(vals) != 6:
+        raise ValueError(f"hash_bounds needs 6 values (lo xyz, hi xyz), got {len(vals)}")
+    return vals
 
 
 class _IntegratePrimitives(Function):
@@ -102,13 +118,18 @@ class _IntegratePrimitives(Function):
             raise ValueError(f"cam_pos must have at least 3 elements, but has shape {cam_pos.shape}")
         cam_pos = cam_pos.contiguous().float()
 
-        num_rendered, out_color, out_features, visibility_info, geom, binning, img = _C.integrate_primitives(
-            means3D, conf_flat, s.primitive_scale, viewmatrix, projmatrix, cam_pos, s.tanfovx, s.tanfovy,
-            s.image_height, s.image_width, s.near_plane, s.max_distance, feature_table, resolution, do_hash,
-            primes, s.feature_offset, linear_weights, linear_bias, s.stencil_genus, s.grid_size,
-            s.max_primitives_per_ray, s.occupancy_threshold, bg_color, s.input_feature_dim,
-            s.output_feature_dim, s.intermediate_feature_dim, s.hashgrid_levels, s.num_output_channels,
-            s.debug)
+        args = (means3D, conf_flat, s.primitive_scale, viewmatrix, projmatrix, cam_pos, s.tanfovx, s.tanfovy,
+                s.image_height, s.image_width, s.near_plane, s.max_distance, feature_table, resolution, do_hash,
+                primes, s.feature_offset, linear_weights, linear_bias, s.stencil_genus, s.grid_size,
+                s.max_primitives_per_ray, s.occupancy_threshold, bg_color, s.input_feature_dim,
+                s.output_feature_dim, s.intermediate_feature_dim, s.hashgrid_levels, s.num_output_channels,
+                s.debug)
+        hb = _hash_bounds(s)
+        if hb is None:
+            res = _C.integrate_primitives(*args)
+        else:
+            res = _C.integrate_primitives_ex(*args, hb)
+        num_rendered, out_color, out_features, visibility_info, geom, binning, img = res
 
         ctx.save_for_backward(means3D, conf_flat, feature_table, linear_weights, linear_bias, viewmatrix,
                               projmatrix, cam_pos, resolution, do_hash, primes, bg_color, geom, binning, img,
@@ -126,13 +147,18 @@ class _IntegratePrimitives(Function):
         needs = ctx.needs_input_grad
         if not any(needs[:5]):
             return (None, None, None, None, None, None)
-        dmeans, dconf, dtable, dW, db = _C.integrate_primitives_backward(
-            grad_out_color.contiguous(), grad_out_features.contiguous(), geom, binning, img, means3D, conf_flat,
-            s.primitive_scale, viewmatrix, projmatrix, cam_pos, s.tanfovx, s.tanfovy, s.image_height,
-            s.image_width, s.near_plane, s.max_distance, feature_table, resolution, do_hash, primes,
-            s.feature_offset, linear_weights, linear_bias, s.stencil_genus, s.grid_size, s.max_primitives_per_ray,
-            s.occupancy_threshold, bg_color, s.input_feature_dim, s.output_feature_dim, s.hashgrid_levels,
-            s.num_output_channels, feature_table.numel(), means3D.shape[0], ctx.num_rendered, s.debug)
+        args = (grad_out_color.contiguous(), grad_out_features.contiguous(), geom, binning, img, means3D,
+                conf_flat, s.primitive_scale, viewmatrix, projmatrix, cam_pos, s.tanfovx, s.tanfovy,
+                s.image_height, s.image_width, s.near_plane, s.max_distance, feature_table, resolution, do_hash,
+                primes, s.feature_offset, linear_weights, linear_bias, s.stencil_genus, s.grid_size,
+                s.max_primitives_per_ray, s.occupancy_threshold, bg_color, s.input_feature_dim,
+                s.output_feature_dim, s.hashgrid_levels, s.num_output_channels, feature_table.numel(),
+                means3D.shape[0], ctx.num_rendered, s.debug)
+        hb = _hash_bounds(s)
+        if hb is None:
+            dmeans, dconf, dtable, dW, db = _C.integrate_primitives_backward(*args)
+        else:
+            dmeans, dconf, dtable, dW, db = _C.integrate_primitives_backward_ex(*args, hb)
         if ctx.original_confidences_shape is not None:
             dconf = dconf.view(ctx.original_confidences_shape)
         return (dmeans if needs[0] else None, dconf if needs[1] else None, dtable if needs[2] else None,
