@@ -480,35 +480,37 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
     }
     __syncwarp();
 
-    // One pass over (class, level) items: gather phi, scatter the table gradient.
-    ItemWalk it(L);
-    for (int base = 0; base < pc.U * L; base += 32, it.next()) {
-      if (it.u < pc.U) {
-        const float4 n4 = npos_s[it.u];
-        const LevelCorners lc = level_corners(make_float3(n4.x, n4.y, n4.z), res_s[it.l], resf_s[it.l],
-                                              hash_s[it.l] != 0, p0, p1, p2, sc.T);
-        const bool doA = (mem_s[it.u] & amask) != 0u;
-        float A[F], acc[F];
+    // One pass over (class, level) items, level by level: gather phi, scatter
+    // the table gradient.  Lanes of one level that hit the same table entry
+    // share one load request and one atomic request.
+    const LevelWalk it(pc.U, L);
+    for (int l0 = 0; l0 < L; l0 += it.per) {
+      if (!it.valid(l0)) continue;
+      const int l = it.level(l0), u = it.u;
+      const float4 n4 = npos_s[u];
+      const LevelCorners lc = level_corners(make_float3(n4.x, n4.y, n4.z), res_s[l], resf_s[l], hash_s[l] != 0,
+                                            p0, p1, p2, sc.T);
+      const bool doA = (mem_s[u] & amask) != 0u;
+      float A[F], acc[F];
 #pragma unroll
-        for (int f = 0; f < F; f++) {
-          acc[f] = 0.0f;
-          // table coefficient of this level: sum_o W[o][l*F+f] S_u[o]
-          float sum = 0.0f;
-          if (doA) {
+      for (int f = 0; f < F; f++) {
+        acc[f] = 0.0f;
+        // table coefficient of this level: sum_o W[o][l*F+f] S_u[o]
+        float sum = 0.0f;
+        if (doA) {
 #pragma unroll
-            for (int o = 0; o < OMAX; o++) sum += W_s[o * DP + it.l * F + f] * S_s[it.u * OMAX + o];
-          }
-          A[f] = sum;
+          for (int o = 0; o < OMAX; o++) sum += W_s[o * DP + l * F + f] * S_s[u * OMAX + o];
         }
-        const float* lvl = sc.table + (size_t)it.l * F;
-        float* dst = dtable + (size_t)it.l * F;
-        if (sc.Tmask)
-          gather_scatter_level<F, true>(lc, lvl, dst, stride, sc.T, sc.Tmask, doA, A, acc);
-        else
-          gather_scatter_level<F, false>(lc, lvl, dst, stride, sc.T, sc.Tmask, doA, A, acc);
-#pragma unroll
-        for (int f = 0; f < F; f++) phi_s[it.u * DP + it.l * F + f] = acc[f];
+        A[f] = sum;
       }
+      const float* lvl = sc.table + (size_t)l * F;
+      float* dst = dtable + (size_t)l * F;
+      if (sc.Tmask)
+        gather_scatter_level<F, true>(lc, lvl, dst, stride, sc.T, sc.Tmask, doA, A, acc);
+      else
+        gather_scatter_level<F, false>(lc, lvl, dst, stride, sc.T, sc.Tmask, doA, A, acc);
+#pragma unroll
+      for (int f = 0; f < F; f++) phi_s[u * DP + l * F + f] = acc[f];
     }
     __syncwarp();
     // W phi per class (into cv_s, free now).

@@ -8,7 +8,7 @@
 // magnitude.  The hashgrid features and the linear layer are then computed once
 // per distinct normalised position rather than once per grid point: lanes are
 // grouped by position, the (position, level) pairs are spread over the warp's
-// lanes, and the linear layer runs over (position, output) pairs.  Lanes that
+// lanes level by level, and the linear layer runs over (position, output) pairs.  Lanes that
 // land in the same pixel are summed in grid-point order by the lowest such lane,
 // exactly the order of the reference's loop, and every pixel whose occupancy sum
 // passes the reference's 1e-7 test becomes one record:
@@ -112,22 +112,23 @@ __global__ void __launch_bounds__(kFeatWarps * 32, 4) features_kernel(Scene sc, 
         npos_s[pc.cls] = make_float4(n.x, n.y, n.z, 0.0f);
       }
       __syncwarp();
-      ItemWalk it(L);
-      for (int base = 0; base < pc.U * L; base += 32, it.next()) {
-        if (it.u < pc.U) {
+      const LevelWalk it(pc.U, L);
+      for (int l0 = 0; l0 < L; l0 += it.per) {
+        if (it.valid(l0)) {
+          const int l = it.level(l0);
           const float4 n4 = npos_s[it.u];
-          const LevelCorners lc = level_corners(make_float3(n4.x, n4.y, n4.z), res_s[it.l], resf_s[it.l],
-                                                hash_s[it.l] != 0, p0, p1, p2, sc.T);
+          const LevelCorners lc = level_corners(make_float3(n4.x, n4.y, n4.z), res_s[l], resf_s[l],
+                                                hash_s[l] != 0, p0, p1, p2, sc.T);
           float acc[F];
 #pragma unroll
           for (int f = 0; f < F; f++) acc[f] = 0.0f;
-          const float* lvl = sc.table + (size_t)it.l * F;
+          const float* lvl = sc.table + (size_t)l * F;
           if (sc.Tmask)
             gather_level<F, true>(lc, lvl, stride, sc.T, sc.Tmask, acc);
           else
             gather_level<F, false>(lc, lvl, stride, sc.T, sc.Tmask, acc);
 #pragma unroll
-          for (int f = 0; f < F; f++) phi_s[it.u * DP + it.l * F + f] = acc[f];
+          for (int f = 0; f < F; f++) phi_s[it.u * DP + l * F + f] = acc[f];
         }
       }
       __syncwarp();

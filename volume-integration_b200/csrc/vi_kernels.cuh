@@ -257,25 +257,21 @@ __device__ __forceinline__ void class_linear(const float* W_s, const float* phi_
   }
 }
 
-// Walks the items (class u, level l), u-major, of a warp: lane i starts at item i
-// and advances by 32 items per step.
-struct ItemWalk {
-  int u, l, su, sl, L;
-  __device__ __forceinline__ explicit ItemWalk(int levels) : L(levels) {
+// Walks the items (class u, level l) of a warp level by level: the lanes form
+// segments of U lanes (lane = segment * U + u), segment j holds level l0 + j,
+// and one step covers per = 32 / U levels.  Lanes of one segment query the same
+// level, so grid points that share table entries share load requests; with
+// U > 16 a step is a single level.
+struct LevelWalk {
+  int per, seg, u, L;
+  __device__ __forceinline__ LevelWalk(int U, int levels) : L(levels) {
     const int lane = (int)(threadIdx.x & 31u);
-    u = lane / L;
-    l = lane - u * L;
-    su = 32 / L;
-    sl = 32 - su * L;
+    per = 32 / U;
+    seg = lane / U;
+    u = lane - seg * U;
   }
-  __device__ __forceinline__ void next() {
-    u += su;
-    l += sl;
-    if (l >= L) {
-      l -= L;
-      u++;
-    }
-  }
+  __device__ __forceinline__ int level(int l0) const { return l0 + seg; }
+  __device__ __forceinline__ bool valid(int l0) const { return seg < per && l0 + seg < L; }
 };
 
 }  // namespace vi
