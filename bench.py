@@ -51,6 +51,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-aabb", action="store_true", help="skip the run with the hashgrid box at the scene bounds")
+    ap.add_argument("--views", default="one", choices=["one", "all"],
+                    help="one: one view per GPU (weak scaling); all: every camera of the scene per step, "
+                         "sharded over the GPUs (strong scaling)")
     return ap.parse_args()
 
 
@@ -88,18 +91,31 @@ def frame_stats(means, conf, s):
     return {"R": int(R), "Pv": int((v["radii"] > 0).sum()), "Kt": int(v["n_contrib"].sum())}
 
 
-def workload(config, rank, world, device):
+def workload(config, rank, world, device, all_views=False):
+    """The scene and this rank's views: [(settings, dL/dcolor, dL/dfeatures)], and
+    the number of views all ranks render per step.  One view per rank (weak
+    scaling; cameras on an orbit when the scene has fewer than the ranks), or
+    with all_views every camera of the scene, sharded over the ranks (strong)."""
     import vi_workloads as wl
+    from volume_integration.distributed import views_for_rank
     means, conf, kw, cams = wl.make(config)
     c = wl.CONFIGS[config]
-    if world > 1 and len(cams) < world:
-        cams = wl.orbit(world, c["dist"], c["width"], c["height"], c["fov"])
-    cam = cams[rank % len(cams)]
-    s = settings_from(kw, cam, device)
-    gen = torch.Generator().manual_seed(77 + rank)
-    dc = torch.randn(3, s.image_height, s.image_width, generator=gen).to(device)
-    df = torch.randn(s.output_feature_dim, s.image_height, s.image_width, generator=gen).to(device)
-    return means.to(device), conf.to(device), s, dc, df
+    if all_views:
+        idx = views_for_rank(len(cams), rank, world)
+        total = len(cams)
+    else:
+        if world > 1 and len(cams) < world:
+            cams = wl.orbit(world, c["dist"], c["width"], c["height"], c["fov"])
+        idx = [rank % len(cams)]
+        total = world
+    views = []
+    for v in idx:
+        s = settings_from(kw, cams[v], device)
+        gen = torch.Generator().manual_seed(77 + v)
+        dc = torch.randn(3, s.image_height, s.image_width, generator=gen).to(device)
+        df = torch.randn(s.output_feature_dim, s.image_height, s.image_width, generator=gen).to(device)
+        views.append((s, dc, df))
+    return means.to(device), conf.to(device), views, total
 
 
 def algorithmic_bytes(st, s, P):
@@ -209,7 +225,10 @@ def run_ours(args):
     from volume_integration import _C
     from volume_integration.distributed import allreduce_gradients
 
-    means, conf, s, dc, df = workload(args.config, rank, world, device)
+    means, conf, views, total_views = workload(args.config, rank, world, device, args.views == "all")
+    if not views:
+        raise SystemExit(f"--views all: the {args.config} scene has fewer cameras than the {world} ranks")
+    s = views[0][0]
     P = means.shape[0]
     confp = conf.clone().requires_grad_(True)
     table = s.feature_table.clone().requires_grad_(True)
@@ -217,14 +236,21 @@ def run_ours(args):
     bl = s.linear_bias.clone().requires_grad_(True)
     leaves = [confp, table, Wl, bl]
 
-    def step(m, c, t, w, b, settings=s):
-        oc, of, vis = vi.integrate_primitives(m, c, t, w, b, settings)
-        grads = torch.autograd.grad([oc, of], [c, t, w, b], [dc, df])
-        allreduce_gradients(grads)  # sum over ranks (no-op with one rank)
-        return oc, of, vis, grads
+    def step(m, c, t, w, b, vlist=views):
+        """Forward + backward of this rank's views, gradients summed over views and ranks."""
+        acc = None
+        for settings, gc, gf in vlist:
+            oc, of, vis = vi.integrate_primitives(m, c, t, w, b, settings)
+            grads = torch.autograd.grad([oc, of], [c, t, w, b], [gc, gf])
+            acc = list(grads) if acc is None else [a.add_(g) for a, g in zip(acc, grads)]
+        if acc is None:  # a rank without views still takes part in the all-reduce
+            acc = [torch.zeros_like(x) for x in (c, t, w, b)]
+        allreduce_gradients(acc)  # sum over ranks (no-op with one rank)
+        return acc
 
-    # workload statistics for the roofline (one forward, outside timing)
-    stats = frame_stats(means, conf, s)
+    # workload statistics for the roofline (one forward per view, outside timing)
+    vstats = [frame_stats(means, conf, sv) for sv, _, _ in views]
+    stats = {k: sum(st[k] for st in vstats) for k in ("R", "Pv", "Kt")}
 
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)  # > 126 MB L2
     clocks = Clocks(device.index)
@@ -258,32 +284,37 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         total_ms = float(t.item())
         dist.barrier()
-    value = world * args.steps / (total_ms / 1000.0)
+    value = total_views * args.steps / (total_ms / 1000.0)
+    nv = max(1, len(views))
 
     # roofline of the dominant stage, timed live on the launching stream
     peak, peak_kind = measured_peaks()
-    ab = algorithmic_bytes(stats, s, P)
+    abv = [algorithmic_bytes(st, sv, P) for st, (sv, _, _) in zip(vstats, views)]
+    ab = {k: sum(a[k] for a in abv) / nv for k in abv[0]} if abv else algorithmic_bytes(stats, s, P)
     stage_ms = {k: v[0] for k, v in prof.items()}
     stage_calls = {k: v[1] for k, v in prof.items()}
     groups = {"features": ["features"], "render": ["render"], "backward": ["bwd_pixel", "bwd_prim"],
               "sort": ["depth_sort", "offsets", "binning"], "preprocess": ["preprocess"]}
     gms = {g: sum(stage_ms[k] for k in ks) for g, ks in groups.items()}
     dom = max(gms, key=gms.get)
-    per_launch_ms = gms[dom] / max(1, args.steps)
+    per_launch_ms = gms[dom] / max(1, args.steps * nv)
     achieved = ab[dom] / (per_launch_ms / 1000.0) / 1e9
     roofline = {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
                 "algorithmic_bytes": int(ab[dom]), "ms_per_launch": round(per_launch_ms, 4)}
     sort_ms = gms["sort"] / max(1, args.steps)
-    sort_gkeys = stats["R"] / (sort_ms / 1000.0) / 1e9 if sort_ms > 0 else None
+    sort_gkeys = stats["R"] / (sort_ms / 1000.0) / 1e9 if sort_ms > 0 else None  # R summed over views
 
     line = {"metric": METRIC, "value": round(value, 3), "unit": "frames/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "scaling": "strong" if args.views == "all" else "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
             "config": {"workload": f"{args.config}: {P} primitives, {s.image_width}x{s.image_height}, "
                                    f"L={s.hashgrid_levels} F={s.input_feature_dim} T=2^{int(math.log2(s.feature_offset))}"
-                                   f", G={s.grid_size}, K={s.max_primitives_per_ray}, one view per GPU",
-                       "global_batch": world, "parallelism": f"views sharded dp{world}",
+                                   f", G={s.grid_size}, K={s.max_primitives_per_ray}, "
+                                   + (f"{total_views} views per step sharded over the GPUs" if args.views == "all"
+                                      else "one view per GPU"),
+                       "global_batch": total_views, "parallelism": f"views sharded dp{world}",
                        "l2": "256 MB buffer written between timed steps",
                        "num_rendered": stats["R"], "visible_primitives": stats["Pv"],
                        "contributions": stats["Kt"]},
@@ -294,10 +325,11 @@ def run_ours(args):
             "clocks": clk}
 
     if not args.no_aabb:
-        line["scene_bounds"] = run_scene_bounds(args, step, means, leaves, s, flush, world, dist, device, _C)
+        line["scene_bounds"] = run_scene_bounds(args, step, means, leaves, views, total_views, flush, world, dist,
+                                                device, _C)
 
     if not args.no_e2e:
-        line["e2e"] = run_e2e(args, vi, means, conf, s, dc, df, world, dist if world > 1 else None, device)
+        line["e2e"] = run_e2e(args, vi, means, conf, views, total_views, world, dist if world > 1 else None, device)
 
     if world > 1:
         dist.barrier()
@@ -308,20 +340,20 @@ def run_ours(args):
         print(json.dumps(line), flush=True)
 
 
-def run_scene_bounds(args, step, means, leaves, s, flush, world, dist, device, _C):
+def run_scene_bounds(args, step, means, leaves, views, total_views, flush, world, dist, device, _C):
     """The same step with the hashgrid box set to the scene's own bounds (an
     extension field).  The reference's fixed [-1.3, 1.3]^3 box clamps most
     positions of this scene to its faces, where grid points share table
     entries; inside its own bounds every grid point of a primitive reads its own
     cells, which is the harder case for the hashgrid kernels."""
     import dataclasses
-    pad = float(s.primitive_scale)
+    pad = float(views[0][0].primitive_scale) if views else 0.0
     lo = (means.min(0).values - pad).tolist()
     hi = (means.max(0).values + pad).tolist()
-    sb = dataclasses.replace(s, hash_bounds=tuple(lo + hi))
+    vb = [(dataclasses.replace(sv, hash_bounds=tuple(lo + hi)), gc, gf) for sv, gc, gf in views]
     steps = max(1, min(args.steps, 50))
     for _ in range(max(3, args.warmup)):
-        step(means, *leaves, settings=sb)
+        step(means, *leaves, vlist=vb)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -331,7 +363,7 @@ def run_scene_bounds(args, step, means, leaves, s, flush, world, dist, device, _
     for i in range(steps):
         flush.zero_()
         ev[i][0].record()
-        step(means, *leaves, settings=sb)
+        step(means, *leaves, vlist=vb)
         ev[i][1].record()
     torch.cuda.synchronize()
     _C.profile_enable(False)
@@ -341,40 +373,49 @@ def run_scene_bounds(args, step, means, leaves, s, flush, world, dist, device, _
         t = torch.tensor([total_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         total_ms = float(t.item())
-    return {"value": round(world * steps / (total_ms / 1000.0), 3), "unit": "frames/s", "steps": steps,
+    return {"value": round(total_views * steps / (total_ms / 1000.0), 3), "unit": "frames/s", "steps": steps,
             "ms_per_step": round(total_ms / steps, 4), "hash_bounds": [round(v, 4) for v in lo + hi],
             "stage_ms_per_step": {k: round(v[0] / steps, 4) for k, v in prof.items()}}
 
 
-def run_e2e(args, vi, means, conf, s, dc, df, world, dist, device):
+def run_e2e(args, vi, means, conf, views, total_views, world, dist, device):
     """Same step through the public API with host inputs: pinned H2D copies of every
-    input and D2H copies of the images and gradients inside the timed region."""
+    input (the scene once, dL/dimage per view) and D2H copies of the images and
+    gradients inside the timed region."""
     from volume_integration.distributed import allreduce_gradients
-    host_in = [t.detach().cpu().pin_memory() for t in (means, conf, s.feature_table, s.linear_weights,
-                                                      s.linear_bias, dc, df)]
-    dev_in = [torch.empty_like(t, device=device) for t in host_in]
+    s = views[0][0]
+    scene = [t.detach().cpu().pin_memory() for t in (means, conf, s.feature_table, s.linear_weights, s.linear_bias)]
+    per_view = [[t.detach().cpu().pin_memory() for t in (gc, gf)] for _, gc, gf in views]
+    dev_scene = [torch.empty_like(t, device=device) for t in scene]
+    dev_views = [[torch.empty_like(t, device=device) for t in pv] for pv in per_view]
     outs = None
-    h2d = sum(t.numel() * t.element_size() for t in host_in)
+    h2d = sum(t.numel() * t.element_size() for t in scene) + \
+        sum(t.numel() * t.element_size() for pv in per_view for t in pv)
 
     def one():
         nonlocal outs
-        for d, h in zip(dev_in, host_in):
+        for d, h in zip(dev_scene, scene):
             d.copy_(h, non_blocking=True)
-        m, c, t, w, b, gc, gf = dev_in
-        c.requires_grad_(True)
-        t.requires_grad_(True)
-        w.requires_grad_(True)
-        b.requires_grad_(True)
-        oc, of, vis = vi.integrate_primitives(m, c, t, w, b, s)
-        grads = torch.autograd.grad([oc, of], [c, t, w, b], [gc, gf])
-        allreduce_gradients(grads)
-        res = [oc.detach(), of.detach(), vis.detach()] + list(grads)
+        for dv, pv in zip(dev_views, per_view):
+            for d, h in zip(dv, pv):
+                d.copy_(h, non_blocking=True)
+        m, c, t, w, b = dev_scene
+        for x in (c, t, w, b):
+            x.requires_grad_(True)
+        res, acc = [], None
+        for (sv, _, _), (gc, gf) in zip(views, dev_views):
+            oc, of, vis = vi.integrate_primitives(m, c, t, w, b, sv)
+            grads = torch.autograd.grad([oc, of], [c, t, w, b], [gc, gf])
+            acc = list(grads) if acc is None else [a.add_(g) for a, g in zip(acc, grads)]
+            res += [oc.detach(), of.detach(), vis.detach()]
+        allreduce_gradients(acc)
+        res += acc
         if outs is None:
             outs = [torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res]
         for o, r in zip(outs, res):
             o.copy_(r, non_blocking=True)
-        for d in dev_in:
-            d.requires_grad_(False)
+        for x in (c, t, w, b):
+            x.requires_grad_(False)
 
     for _ in range(max(1, args.warmup)):
         one()
@@ -393,7 +434,7 @@ def run_e2e(args, vi, means, conf, s, dc, df, world, dist, device):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     d2h = sum(o.numel() * o.element_size() for o in outs)
-    return {"value": round(world * args.steps / (ms / 1000.0), 3), "unit": "frames/s",
+    return {"value": round(total_views * args.steps / (ms / 1000.0), 3), "unit": "frames/s",
             "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)}
 
 

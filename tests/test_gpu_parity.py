@@ -195,3 +195,15 @@ def test_hash_bounds_rejects_an_empty_box():
     s = dataclasses.replace(s, hash_bounds=(0.0, 0.0, 0.0, 1.0, -1.0, 1.0))
     with pytest.raises(RuntimeError, match="hash_bounds"):
         vi.integrate_primitives(means, conf, s.feature_table, s.linear_weights, s.linear_bias, s)
+
+
+# The backward reads the hashgrid features of each position class from a cache
+# the feature stage fills; primitives that find no room gather them again.
+# VI_PHI_CACHE_BYTES bounds the cache: 0 = no cache, a small bound = a mix.
+@pytest.mark.parametrize("limit", ["0", "20000"])
+def test_feature_cache_fallback(limit, monkeypatch):
+    monkeypatch.setenv("VI_PHI_CACHE_BYTES", limit)
+    means, conf, s = tl.custom_scene(seed=21, P=400, extent=1.0)
+    _check(means, conf, s, seed=7)
+    means, conf, s = tl.scene("tiny", table_range=1.0)
+    _check(means, conf, s, seed=8)

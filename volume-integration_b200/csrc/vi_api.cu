@@ -3,6 +3,7 @@
 // cuda_integrator/integrator_impl.cu:196-469 and :474-756).
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstdarg>
 #include <mutex>
@@ -10,6 +11,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 
 #include "../../include/volume_integration_b200.h"
@@ -117,7 +119,15 @@ void stage_end(Stage st, cudaStream_t s) {
   g_open[st] = nullptr;
 }
 
-GeomState geom_layout(char* base, size_t P, int V, int O) {
+size_t phi_cache_max_bytes() {
+  const char* e = std::getenv("VI_PHI_CACHE_BYTES");
+  if (!e || !*e) return kPhiCacheMaxBytes;
+  char* end = nullptr;
+  const unsigned long long v = std::strtoull(e, &end, 10);
+  return (end && *end == '\0') ? (size_t)v : kPhiCacheMaxBytes;
+}
+
+GeomState geom_layout(char* base, size_t P, int V, int O, int D) {
   GeomState g;
   Carver c(base);
   const int OP = props_stride(O);
@@ -139,6 +149,12 @@ GeomState geom_layout(char* base, size_t P, int V, int O) {
   g.rec_dpre = c.take<float>(P * V * OP);
   char* st = c.take<char>(sort_temp_bytes(P, 4, 0, 32));
   sort_temp_carve(st, P, 4, 0, 32, g.sort);
+  // Last, so the offsets above do not depend on D.
+  g.cls_base = c.take<uint32_t>(P);
+  const size_t want = P * (size_t)V;
+  const size_t cap = D > 0 ? std::min(want, phi_cache_max_bytes() / (sizeof(float) * (size_t)D)) : 0;
+  g.phi_cap = (uint32_t)cap;
+  g.phi_cache = c.take<float>(cap * (size_t)D);
   g.bytes = c.size();
   return g;
 }
@@ -301,11 +317,11 @@ int forward_impl(
   }
   const size_t tiles = (size_t)sc.gx * sc.gy;
 
-  GeomState g = geom_layout(nullptr, P, sc.V, sc.O);
+  GeomState g = geom_layout(nullptr, P, sc.V, sc.O, sc.D);
   char* gb = geom_buffer(geom_user, g.bytes);
   if (!gb) return fail(VI_ERR_ALLOC, "geometry buffer of %zu bytes", g.bytes);
   if ((uintptr_t)gb & 255) return fail(VI_ERR_INVALID_ARGUMENT, "state buffers must be 256-byte aligned");
-  g = geom_layout(gb, P, sc.V, sc.O);
+  g = geom_layout(gb, P, sc.V, sc.O, sc.D);
   ImgState im = img_layout(nullptr, N, sc.K, tiles);
   char* ib = img_buffer(img_user, im.bytes);
   if (!ib) return fail(VI_ERR_ALLOC, "image buffer of %zu bytes", im.bytes);
@@ -413,7 +429,7 @@ int backward_impl(
   if (((uintptr_t)feature_table) % (size_t)(sc.F >= 4 ? 16 : sc.F * 4) != 0 ||
       ((uintptr_t)dL_dfeature_table) % (size_t)(sc.F >= 4 ? 16 : sc.F * 4) != 0)
     return fail(VI_ERR_INVALID_ARGUMENT, "feature_table and its gradient must be aligned to one entry's vector");
-  GeomState g = geom_layout(geom_buffer, P, sc.V, sc.O);
+  GeomState g = geom_layout(geom_buffer, P, sc.V, sc.O, sc.D);
   ImgState im = img_layout(img_buffer, N, sc.K, (size_t)sc.gx * sc.gy);
   launch_backward(sc, g, im, dL_dout_color, sc.Fout ? dL_dout_features : nullptr, dL_dconfidences,
                   dL_dfeature_table, dL_dlinear_weights, dL_dlinear_bias, s);
@@ -543,7 +559,7 @@ extern "C" int vi_get_state_layout(int P, int64_t num_rendered, int image_height
   const int V = grid_size * grid_size * grid_size, O = (int)output_feature_dim + 4;
   const size_t N = (size_t)image_width * image_height;
   const size_t tiles = (size_t)((image_width + 15) / 16) * ((image_height + 15) / 16);
-  GeomState g = geom_layout(nullptr, P, V, O);
+  GeomState g = geom_layout(nullptr, P, V, O, 0);
   const int tb = tile_bits(tiles);
   BinState b = bin_layout(nullptr, (uint64_t)num_rendered, tb);
   ImgState m = img_layout(nullptr, N, max_primitives_per_ray, tiles);
@@ -573,7 +589,7 @@ extern "C" int vi_get_state_layout(int P, int64_t num_rendered, int image_height
 }
 
 extern "C" int vi_read_device_status(const char* geom_buffer, uint32_t* status, void* stream) {
-  GeomState g = geom_layout((char*)geom_buffer, 0, 1, 4);
+  GeomState g = geom_layout((char*)geom_buffer, 0, 1, 4, 0);
   cudaError_t e = cudaMemcpyAsync(status, g.status, 4, cudaMemcpyDeviceToHost, (cudaStream_t)stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
   return e == cudaSuccess ? VI_OK : cuda_fail(e, "read status");

@@ -241,6 +241,34 @@ __device__ __forceinline__ void gather_scatter_level(const LevelCorners& c, cons
   }
 }
 
+// The scatter half of gather_scatter_level: A[f] * (corner weight) into the
+// table gradient at each corner of one (position, level) query.
+template <int F, bool POW2>
+__device__ __forceinline__ void scatter_level(const LevelCorners& c, float* __restrict__ dst, uint32_t stride,
+                                              uint32_t T, uint32_t Tmask, const float* A) {
+  const uint32_t hxy[4] = {c.hsh ? c.ix0 ^ c.iy0 : c.ix0 + c.iy0, c.hsh ? c.ix0 ^ c.iy1 : c.ix0 + c.iy1,
+                           c.hsh ? c.ix1 ^ c.iy0 : c.ix1 + c.iy0, c.hsh ? c.ix1 ^ c.iy1 : c.ix1 + c.iy1};
+  const float wxy[4] = {c.wx0 * c.wy0, c.wx0 * c.wy1, c.wx1 * c.wy0, c.wx1 * c.wy1};
+#pragma unroll
+  for (int k = 0; k < 8; k++) {
+    if ((c.mask >> k) & 1u) {
+      const uint32_t z = (k & 1) ? c.iz1 : c.iz0;
+      uint32_t e;
+      if (c.hsh) {
+        const uint32_t h = hxy[k >> 1] ^ z;
+        e = POW2 ? (h & Tmask) : (h % T);
+      } else {
+        e = hxy[k >> 1] + z;
+      }
+      const float w = wxy[k >> 1] * ((k & 1) ? c.wz1 : c.wz0);
+      float x[F];
+#pragma unroll
+      for (int f = 0; f < F; f++) x[f] = A[f] * w;
+      atomic_vec<F>(dst + (size_t)e * stride, x);
+    }
+  }
+}
+
 // One warp per primitive, lane g = grid point g.  With dIn_p = W^T dpre_p
 // (backward.cu:608-619), every per-pair sum collapses onto O-wide vectors:
 //   v_g  = sum_p g'_{p,g} dpre_p                 -> dconf_g = v_g . (W phi_g)
@@ -431,11 +459,17 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
     }
 #pragma unroll
     for (int o = 0; o < OMAX; o++) cv_s[lane * OMAX + o] = hasA ? conf * vA[o] : 0.0f;
+    // With the forward's class features (phi_cache) the classes are those of
+    // all grid points, as in the feature stage; otherwise those of the
+    // gathering lanes only.
+    const uint32_t cb = g.cls_base[q];
+    const bool cached = cb != kNoCache;
+    const bool member = cached ? act : gather;
     const float3 nrm = hash_norm(pos, sc.hlo, sc.hext);
-    const PosClasses pc = pos_classes(nrm, gather);
+    const PosClasses pc = pos_classes(nrm, member);
     const uint32_t amask = __ballot_sync(0xffffffffu, hasA);
     const uint32_t emask = __ballot_sync(0xffffffffu, hasE);
-    if (gather && (pc.peers & lt_mask) == 0u) {
+    if (member && (pc.peers & lt_mask) == 0u) {
       npos_s[pc.cls] = make_float4(nrm.x, nrm.y, nrm.z, 0.0f);
       mem_s[pc.cls] = pc.peers;
     }
@@ -480,17 +514,22 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
     }
     __syncwarp();
 
-    // One pass over (class, level) items, level by level: gather phi, scatter
-    // the table gradient.  Lanes of one level that hit the same table entry
-    // share one load request and one atomic request.
+    if (cached) {
+      const float* src = g.phi_cache + (size_t)cb * D;
+      for (int i = (int)lane; i < pc.U * D; i += 32) phi_s[(i / D) * DP + i % D] = src[i];
+    }
+    // One pass over (class, level) items, level by level: scatter the table
+    // gradient, and gather phi unless the forward cached it.  Lanes of one
+    // level that hit the same table entry share one request.
     const LevelWalk it(pc.U, L);
     for (int l0 = 0; l0 < L; l0 += it.per) {
       if (!it.valid(l0)) continue;
       const int l = it.level(l0), u = it.u;
+      const bool doA = (mem_s[u] & amask) != 0u;
+      if (cached && !doA) continue;
       const float4 n4 = npos_s[u];
       const LevelCorners lc = level_corners(make_float3(n4.x, n4.y, n4.z), res_s[l], resf_s[l], hash_s[l] != 0,
                                             p0, p1, p2, sc.T);
-      const bool doA = (mem_s[u] & amask) != 0u;
       float A[F], acc[F];
 #pragma unroll
       for (int f = 0; f < F; f++) {
@@ -505,6 +544,13 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
       }
       const float* lvl = sc.table + (size_t)l * F;
       float* dst = dtable + (size_t)l * F;
+      if (cached) {
+        if (sc.Tmask)
+          scatter_level<F, true>(lc, dst, stride, sc.T, sc.Tmask, A);
+        else
+          scatter_level<F, false>(lc, dst, stride, sc.T, sc.Tmask, A);
+        continue;
+      }
       if (sc.Tmask)
         gather_scatter_level<F, true>(lc, lvl, dst, stride, sc.T, sc.Tmask, doA, A, acc);
       else

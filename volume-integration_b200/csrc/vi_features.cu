@@ -78,7 +78,10 @@ __global__ void __launch_bounds__(kFeatWarps * 32, 4) features_kernel(Scene sc, 
   for (int q = blockIdx.x * kFeatWarps + w; q < sc.P; q += nwarps) {
     const int r = g.radii[q];
     if (r <= 0) {
-      if (lane == 0) g.rec_cnt[q] = 0;
+      if (lane == 0) {
+        g.rec_cnt[q] = 0;
+        g.cls_base[q] = kNoCache;
+      }
       continue;
     }
     const float3 c = make_float3(sc.means[3 * q], sc.means[3 * q + 1], sc.means[3 * q + 2]);
@@ -104,10 +107,12 @@ __global__ void __launch_bounds__(kFeatWarps * 32, 4) features_kernel(Scene sc, 
     const bool vpt = act && conf > 0.0f && inside && tx >= x0 && tx < x1 && ty >= y0 && ty < y1;
     const bool need = vpt && mag > 1e-7f;
 
+    uint32_t cbase = kNoCache;
     if (__any_sync(0xffffffffu, need)) {
-      // Features of each distinct position: items (class u, level l) over the lanes.
-      const PosClasses pc = pos_classes(hash_norm(pos, sc.hlo, sc.hext), need);
-      if (need && (pc.peers & lt_mask) == 0) {
+      // Features of each distinct position of all grid points (the backward
+      // reads them from phi_cache): items (class u, level l) over the lanes.
+      const PosClasses pc = pos_classes(hash_norm(pos, sc.hlo, sc.hext), act);
+      if (act && (pc.peers & lt_mask) == 0) {
         const float3 n = hash_norm(pos, sc.hlo, sc.hext);
         npos_s[pc.cls] = make_float4(n.x, n.y, n.z, 0.0f);
       }
@@ -132,6 +137,17 @@ __global__ void __launch_bounds__(kFeatWarps * 32, 4) features_kernel(Scene sc, 
         }
       }
       __syncwarp();
+      // Keep the classes' features for the backward: U consecutive slots of
+      // phi_cache from a counter (status[6]), when they fit.
+      if (lane == 0) {
+        const uint32_t b = atomicAdd(g.status + 6, (uint32_t)pc.U);
+        cbase = (uint64_t)b + (uint64_t)pc.U <= (uint64_t)g.phi_cap ? b : kNoCache;
+      }
+      cbase = __shfl_sync(0xffffffffu, cbase, 0);
+      if (cbase != kNoCache) {
+        float* dst = g.phi_cache + (size_t)cbase * D;
+        for (int i = lane; i < pc.U * D; i += 32) dst[i] = phi_s[(i / D) * DP + i % D];
+      }
       // Linear layer per class: mlp[u][o] = sum_i W[o][i] phi_u[i].
       class_linear<OMAX>(W_s, phi_s, DP, D, pc.U, mlp_s);
       if (need) {
@@ -199,7 +215,10 @@ __global__ void __launch_bounds__(kFeatWarps * 32, 4) features_kernel(Scene sc, 
       for (int o4 = 0; o4 < OMAX / 4; o4++)
         dst[o4] = make_float4(props[4 * o4], props[4 * o4 + 1], props[4 * o4 + 2], props[4 * o4 + 3]);
     }
-    if (lane == 0) g.rec_cnt[q] = (uint32_t)__popc(recmask) | (differs ? kBwdDiffers : 0u);
+    if (lane == 0) {
+      g.rec_cnt[q] = (uint32_t)__popc(recmask) | (differs ? kBwdDiffers : 0u);
+      g.cls_base[q] = cbase;
+    }
     __syncwarp();
   }
 }

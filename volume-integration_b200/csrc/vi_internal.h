@@ -44,7 +44,7 @@ bool onesweep_sort_u64(uint64_t* keys, uint32_t* vals, uint64_t* alt_keys, uint3
 // Geometry state: everything sized by the primitive count P.
 // ---------------------------------------------------------------------------
 struct GeomState {
-  uint32_t* status;          // [0] status bits, [2..3] num_rendered as u64, [4] [5] work counters
+  uint32_t* status;          // [0] status bits, [2..3] num_rendered as u64, [4] [5] work counters, [6] phi_cache slots used
   float* depths;             // [P] view-space z of the centre
   int* radii;                // [P]
   float* means2D;            // [2P]
@@ -61,11 +61,22 @@ struct GeomState {
   uint32_t* rec_pix;         // [P*V] pixel + 1 of a contributing record, 0 otherwise (backward)
   float* rec_dpre;           // [P*V*O] dL/d(pre-activation) per contributing record
   SortTemp sort;
+  uint32_t* cls_base;        // [P] first slot of the primitive's position classes in phi_cache, or kNoCache
+  float* phi_cache;          // [phi_cap][D] hashgrid features of each position class (feature stage)
+  uint32_t phi_cap;          // slots in phi_cache
   size_t bytes;
 };
+constexpr uint32_t kNoCache = 0xffffffffu;
+// Upper bound of phi_cache: every position class of every primitive when that
+// fits, else this many bytes (primitives that find no room gather in the
+// backward).  The environment variable VI_PHI_CACHE_BYTES overrides it (0 turns
+// the cache off); it is read at every call, and the backward does not need the
+// value the forward used, since phi_cache is the last array of the layout.
+constexpr size_t kPhiCacheMaxBytes = 8ull << 30;
+size_t phi_cache_max_bytes();
 constexpr uint32_t kBwdDiffers = 0x80000000u;
 constexpr int kScanBlock = 2048;
-GeomState geom_layout(char* base, size_t P, int V, int O);
+GeomState geom_layout(char* base, size_t P, int V, int O, int D);
 
 // Binning state: everything sized by the overlap count R.
 struct BinState {
