@@ -118,6 +118,20 @@ def workload(config, rank, world, device, all_views=False):
     return means.to(device), conf.to(device), views, total
 
 
+def measured_traffic(config, group):
+    """DRAM bytes per launch of a stage group, from the ncu capture committed under
+    profiles/ for this workload (None when there is none)."""
+    path = os.path.join(ROOT, "profiles", f"dram_traffic_{config}.json")
+    if not os.path.exists(path):
+        return None, None
+    d = json.load(open(path))
+    ks = d.get("groups", {}).get(group)
+    if not ks or any(k not in d["kernels"] for k in ks):
+        return None, None
+    b = sum(d["kernels"][k]["dram_read"] + d["kernels"][k]["dram_write"] for k in ks)
+    return int(b), f"profiles/dram_traffic_{config}.json (ncu dram__bytes_read+write, {', '.join(ks)})"
+
+
 def algorithmic_bytes(st, s, P):
     """Compulsory bytes per stage (fixed formulas, independent of the implementation)."""
     V = s.grid_size ** 3
@@ -299,9 +313,10 @@ def run_ours(args):
     dom = max(gms, key=gms.get)
     per_launch_ms = gms[dom] / max(1, args.steps * nv)
     achieved = ab[dom] / (per_launch_ms / 1000.0) / 1e9
+    traffic, traffic_src = measured_traffic(args.config, dom)
     roofline = {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
-                "algorithmic_bytes": int(ab[dom]), "ms_per_launch": round(per_launch_ms, 4)}
+                "frac": round(achieved / peak, 4), "traffic": traffic, "traffic_source": traffic_src,
+                "peak_kind": peak_kind, "algorithmic_bytes": int(ab[dom]), "ms_per_launch": round(per_launch_ms, 4)}
     sort_ms = gms["sort"] / max(1, args.steps)
     sort_gkeys = stats["R"] / (sort_ms / 1000.0) / 1e9 if sort_ms > 0 else None  # R summed over views
 
@@ -321,6 +336,9 @@ def run_ours(args):
             "roofline": roofline,
             "stage_ms_per_step": {k: round(v / max(1, args.steps), 4) for k, v in stage_ms.items()},
             "sort_gkeys_per_s": round(sort_gkeys, 3) if sort_gkeys else None,
+            # logical hashgrid lookups (8 corners x L levels x V grid points of each visible primitive)
+            "hash_lookups_per_s_per_gpu": round(8 * s.hashgrid_levels * s.grid_size ** 3 * stats["Pv"] * args.steps
+                                        / (total_ms / 1000.0), 1),
             "gpu_launches": int(launches), "gpu_launches_per_step": round(launches / args.steps, 2),
             "clocks": clk}
 

@@ -123,21 +123,34 @@ __global__ void __launch_bounds__(256) backward_pixel_kernel(Scene sc, GeomState
   for (int f = 0; f < OMAX - 4; f++)
     if (f < Fout) dOut[3 + f] = dL_dfeat ? dL_dfeat[f * N + pix] : 0.0f;
   const int px = (int)(pix % sc.W), py = (int)(pix / sc.W);
-  for (int k = nc - 1; k >= 0; k--) {
-    const uint32_t rec = im.contrib_rec[pix * K + k];
-    const float dt = im.delta_t[pix * K + k];
-    const uint32_t q = rec / V;
-    float props[OMAX];
-    if (g.rec_cnt[q] & kBwdDiffers) {
-      recompute_props<OMAX>(sc, q, px, py, props);
-    } else {
-      const float4* src = reinterpret_cast<const float4*>(g.rec_props + (size_t)rec * OMAX);
+  // Contributors are visited in reverse; the record slot, delta t and
+  // properties of the next one are loaded while the current one is processed.
+  const uint32_t* crec = im.contrib_rec + pix * K;
+  const float* cdt = im.delta_t + pix * K;
+  uint32_t r_next = crec[nc - 1];
+  float dt_next = cdt[nc - 1];
+  float4 pn[OMAX / 4];
+  {
+    const float4* src = reinterpret_cast<const float4*>(g.rec_props + (size_t)(r_next & ~kBwdDiffers) * OMAX);
 #pragma unroll
-      for (int o4 = 0; o4 < OMAX / 4; o4++) {
-        float4 v = src[o4];
-        props[4 * o4] = v.x; props[4 * o4 + 1] = v.y; props[4 * o4 + 2] = v.z; props[4 * o4 + 3] = v.w;
-      }
+    for (int o4 = 0; o4 < OMAX / 4; o4++) pn[o4] = src[o4];
+  }
+  for (int k = nc - 1; k >= 0; k--) {
+    const uint32_t r = r_next, rec = r & ~kBwdDiffers;
+    const float dt = dt_next;
+    float props[OMAX];
+#pragma unroll
+    for (int o4 = 0; o4 < OMAX / 4; o4++) {
+      props[4 * o4] = pn[o4].x; props[4 * o4 + 1] = pn[o4].y; props[4 * o4 + 2] = pn[o4].z; props[4 * o4 + 3] = pn[o4].w;
     }
+    if (k > 0) {
+      r_next = crec[k - 1];
+      dt_next = cdt[k - 1];
+      const float4* src = reinterpret_cast<const float4*>(g.rec_props + (size_t)(r_next & ~kBwdDiffers) * OMAX);
+#pragma unroll
+      for (int o4 = 0; o4 < OMAX / 4; o4++) pn[o4] = src[o4];
+    }
+    if (r & kBwdDiffers) recompute_props<OMAX>(sc, rec / V, px, py, props);
     float dens = 0.0f;
 #pragma unroll
     for (int o = 0; o < OMAX; o++)

@@ -96,7 +96,7 @@ struct ImgState {
   int32_t* n_contrib;     // [N]
   int32_t* contrib_idx;   // [N*K] index into the sorted overlap list
   float* delta_t;         // [N*K]
-  uint32_t* contrib_rec;  // [N*K] record slot of the contribution
+  uint32_t* contrib_rec;  // [N*K] record slot of the contribution | kBwdDiffers of its primitive
   size_t bytes;
 };
 ImgState img_layout(char* base, size_t N, int K, size_t tiles);

@@ -37,6 +37,7 @@ __global__ void __launch_bounds__(VI_TILE_PIX) render_kernel(Scene sc, const uin
   __shared__ uint8_t slot[VI_TILE_PIX * kBatch];
   __shared__ uint32_t ent_rec[kBatch];
   __shared__ uint32_t ent_len[kBatch];
+  __shared__ uint32_t ent_flag[kBatch];  // kBwdDiffers of the entry's primitive
   __shared__ float ent_depth[kBatch];
 
   const int tid = threadIdx.x;
@@ -53,7 +54,7 @@ __global__ void __launch_bounds__(VI_TILE_PIX) render_kernel(Scene sc, const uin
   for (int f = 0; f < OMAX - 4; f++) Fe[f] = 0.0f;
   int cnt = 0;
   bool done = !inside, has_p = false;
-  uint32_t pend_rec = 0, pend_gidx = 0;
+  uint32_t pend_rec = 0, pend_gidx = 0, pend_flag = 0;
   float pend_depth = sc.near_plane, T_pend = 0.0f;
 
   const uint32_t r0 = ranges[2 * tile], r1 = ranges[2 * tile + 1];
@@ -74,7 +75,7 @@ __global__ void __launch_bounds__(VI_TILE_PIX) render_kernel(Scene sc, const uin
     const size_t w = pix * K + cnt;
     contrib_idx[w] = (int32_t)pend_gidx;
     delta_t[w] = dt;
-    contrib_rec[w] = pend_rec;
+    contrib_rec[w] = pend_rec | pend_flag;  // the backward's recompute flag rides in bit 31
     cnt++;
   };
 
@@ -83,7 +84,8 @@ __global__ void __launch_bounds__(VI_TILE_PIX) render_kernel(Scene sc, const uin
     const int nb = (int)min((uint32_t)kBatch, r1 - base);
     if (tid < nb) {
       const uint32_t q = point_list[base + tid];
-      const uint32_t n = rec_cnt[q] & ~kBwdDiffers;
+      const uint32_t rc = rec_cnt[q], n = rc & ~kBwdDiffers;
+      ent_flag[tid] = rc & kBwdDiffers;
       const uint32_t* keys = rec_key + (size_t)q * V;
       uint32_t lo = 0, hi = n;  // first record with key >= klo
       while (lo < hi) {
@@ -124,6 +126,7 @@ __global__ void __launch_bounds__(VI_TILE_PIX) render_kernel(Scene sc, const uin
         }
         if (T >= 1e-4f && cnt < K) {
           pend_rec = rec;
+          pend_flag = ent_flag[e];
           pend_depth = depth;
           pend_gidx = base + e;
           has_p = true;
