@@ -334,6 +334,11 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
   const uint32_t lt_mask = (1u << lane) - 1u;
   const uint32_t stride = (uint32_t)D;
   float dbacc = 0.0f;
+  // dW column `lane` (the first 32 columns) accumulates in registers; columns
+  // 32.. (D > 32) in the warp's shared dWw.
+  float dwr[OMAX];
+#pragma unroll
+  for (int o = 0; o < OMAX; o++) dwr[o] = 0.0f;
 
   // Primitives are handed out in batches of kGrab per warp from a counter
   // (status[5]): warps that draw cheap primitives take more, so no warp idles at
@@ -589,7 +594,19 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
     if (emask) {
       for (int u = 0; u < pc.U; u++) {
         if ((mem_s[u] & emask) == 0u) continue;
-        for (int jj = (int)lane; jj < D; jj += 32) {
+        const float4* er = reinterpret_cast<const float4*>(Es_s + u * OMAX);
+        if ((int)lane < D) {
+          const float x = phi_s[u * DP + lane];
+#pragma unroll
+          for (int o4 = 0; o4 < OMAX / 4; o4++) {
+            const float4 e4 = er[o4];
+            dwr[4 * o4] += e4.x * x;
+            dwr[4 * o4 + 1] += e4.y * x;
+            dwr[4 * o4 + 2] += e4.z * x;
+            dwr[4 * o4 + 3] += e4.w * x;
+          }
+        }
+        for (int jj = (int)lane + 32; jj < D; jj += 32) {
           const float x = phi_s[u * DP + jj];
 #pragma unroll
           for (int o = 0; o < OMAX; o++) dWw[o * D + jj] += Es_s[u * OMAX + o] * x;
@@ -600,6 +617,10 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
   }
 
   // CTA reduction of dW and db, then one global atomic per element.
+  if ((int)lane < D) {
+#pragma unroll
+    for (int o = 0; o < OMAX; o++) dWw[o * D + lane] = dwr[o];
+  }
   __syncwarp();
   if ((int)lane < O && dbacc != 0.0f) atomicAdd(&db_s[lane], dbacc);
   __syncthreads();
