@@ -51,6 +51,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-aabb", action="store_true", help="skip the run with the hashgrid box at the scene bounds")
+    ap.add_argument("--exact-gradients", action="store_true",
+                    help="exact-gradient backward (extension) instead of the reference's formula")
     ap.add_argument("--views", default="one", choices=["one", "all"],
                     help="one: one view per GPU (weak scaling); all: every camera of the scene per step, "
                          "sharded over the GPUs (strong scaling)")
@@ -240,6 +242,9 @@ def run_ours(args):
     from volume_integration.distributed import allreduce_gradients
 
     means, conf, views, total_views = workload(args.config, rank, world, device, args.views == "all")
+    if args.exact_gradients:
+        import dataclasses
+        views = [(dataclasses.replace(sv, exact_gradients=True), gc, gf) for sv, gc, gf in views]
     if not views:
         raise SystemExit(f"--views all: the {args.config} scene has fewer cameras than the {world} ranks")
     s = views[0][0]
@@ -330,6 +335,7 @@ def run_ours(args):
                                    + (f"{total_views} views per step sharded over the GPUs" if args.views == "all"
                                       else "one view per GPU"),
                        "global_batch": total_views, "parallelism": f"views sharded dp{world}",
+                       "gradients": "exact (extension)" if args.exact_gradients else "reference formula",
                        "l2": "256 MB buffer written between timed steps",
                        "num_rendered": stats["R"], "visible_primitives": stats["Pv"],
                        "contributions": stats["Kt"]},

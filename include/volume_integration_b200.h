@@ -89,15 +89,25 @@ int vi_integrate_primitives_backward(
     uint64_t feature_table_size, int P, int num_rendered, int debug, void* stream);
 
 /*
- * The two calls above with a hashgrid box other than the reference's fixed
- * [-1.3, 1.3]^3 (reference: hashgrid.h:23-24, :125-126, :225-226).  No
- * counterpart in the reference: scenes larger than that box clamp most
- * positions to its faces, and this lets them use their own bounds.
- * hash_bounds: host pointer to 6 floats {lo_x, lo_y, lo_z, hi_x, hi_y, hi_z}
- * with lo < hi per axis, or NULL for the reference's box.  Positions normalise
- * as clamp((p - lo) / (hi - lo), 0, 1).  The backward must get the bounds the
- * forward got.
+ * The two calls above with two extensions, neither with a counterpart in the
+ * reference:
+ *
+ * hash_bounds: a hashgrid box other than the reference's fixed [-1.3, 1.3]^3
+ *   (reference: hashgrid.h:23-24, :125-126, :225-226).  Scenes larger than that
+ *   box clamp most positions to its faces; this lets them use their own
+ *   bounds.  Host pointer to 6 floats {lo_x, lo_y, lo_z, hi_x, hi_y, hi_z}
+ *   with lo < hi per axis, or NULL for the reference's box.  Positions
+ *   normalise as clamp((p - lo) / (hi - lo), 0, 1).
+ * flags: VI_FLAG_EXACT_GRADIENTS makes the backward the derivative of the
+ *   forward (the reference's backward is not: no transmittance factor, another
+ *   occupancy, no delta-t terms), including dL/dmeans3D through the depths and
+ *   the hashgrid's spatial derivative, and dL/dvisibility
+ *   (dL_dvisibility, [H*W] or NULL).  The forward then keeps two more arrays
+ *   per contribution in the image buffer.
+ *
+ * The backward must get the bounds and flags the forward got.
  */
+#define VI_FLAG_EXACT_GRADIENTS 1u
 int vi_integrate_primitives_ex(
     vi_resize_fn geom_buffer, void* geom_user, vi_resize_fn binning_buffer, void* binning_user,
     vi_resize_fn img_buffer, void* img_user, float* out_color, float* out_features, float* visibility_info,
@@ -109,7 +119,7 @@ int vi_integrate_primitives_ex(
     uint64_t linear_bias_numel, int stencil_genus, int grid_size, int max_primitives_per_ray,
     float occupancy_threshold, const float* bg_color, unsigned input_feature_dim, unsigned output_feature_dim,
     unsigned intermediate_feature_dim, unsigned hashgrid_levels, unsigned num_output_channels, int debug,
-    void* stream, const float* hash_bounds);
+    void* stream, const float* hash_bounds, unsigned flags);
 int vi_integrate_primitives_backward_ex(
     float* dL_dmeans3D, float* dL_dconfidences, float* dL_dfeature_table, float* dL_dlinear_weights,
     float* dL_dlinear_bias, const float* dL_dout_color, const float* dL_dout_features, char* geom_buffer,
@@ -120,7 +130,8 @@ int vi_integrate_primitives_backward_ex(
     const float* linear_weights, const float* linear_bias, int stencil_genus, int grid_size,
     int max_primitives_per_ray, float occupancy_threshold, const float* bg_color, unsigned input_feature_dim,
     unsigned output_feature_dim, unsigned hashgrid_levels, unsigned num_output_channels,
-    uint64_t feature_table_size, int P, int num_rendered, int debug, void* stream, const float* hash_bounds);
+    uint64_t feature_table_size, int P, int num_rendered, int debug, void* stream, const float* hash_bounds,
+    unsigned flags, const float* dL_dvisibility);
 
 /* Frustum test per primitive (view-space z > 0.2).  Replaces markVisible
  * (reference: integrate_primitives.h:136-139, integrate_primitives.cu:436-462). */

@@ -63,6 +63,8 @@ def _declare(l):
     l.vio_render.argtypes = [ctypes.POINTER(Params), vp, vp, vp, i, vp, vp, vp, vp, vp, vp, vp, vp]
     l.vio_backward.argtypes = [ctypes.POINTER(Params), vp, vp, u64, vp, i, vp, vp, vp, vp, vp,
                                vp, vp, vp, vp]
+    l.vio_record_lanes.restype = i
+    l.vio_record_lanes.argtypes = [ctypes.POINTER(Params), ctypes.c_uint32, ctypes.c_uint, ctypes.c_uint, vp, vp]
 
 
 def _p(a):
@@ -259,3 +261,15 @@ def forward(s, tile_mask=None, threads=0):
     res.update(b)
     res.update(out)
     return res
+
+
+def record_lanes(s, q, px, py):
+    """Grid points of primitive q forming its record at pixel (px, py) in the
+    forward, with their stencil magnitudes (test helper for the exact-gradient
+    mode; vio_record_lanes)."""
+    V = s.G ** 3
+    lanes = np.zeros(V, np.int32)
+    mags = np.zeros(V, np.float32)
+    p = s.params()
+    n = lib().vio_record_lanes(ctypes.byref(p), int(q), int(px), int(py), _p(lanes), _p(mags))
+    return lanes[:n].copy(), mags[:n].copy()

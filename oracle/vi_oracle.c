@@ -396,6 +396,38 @@ static float occ_mag_pix(const f2 *scr, int G, int g, int S, const float *cf, un
 
 static float sigm(float x) { return 1.0f / (1.0f + expf(-x)); }
 
+/* Test helper for the exact-gradient mode: the grid points of primitive q that
+ * form its record at pixel (px, py) in the forward (forward projection, conf > 0,
+ * stencil magnitude > 1e-7; forward.cu:481-627) and their magnitudes.  Returns
+ * their count; lanes/mags hold at least G^3 entries.  Not part of the reference. */
+int vio_record_lanes(const vio_params *p, uint32_t q, unsigned px, unsigned py, int32_t *lanes, float *mags) {
+    int G = p->G, V = G * G * G, S, n = 0;
+    float cf[5];
+    stencil(p->genus, &S, cf);
+    f3 c = {p->means[3 * q], p->means[3 * q + 1], p->means[3 * q + 2]};
+    float step = G > 1 ? p->scale / (float)(G - 1) : p->scale;
+    float gof = (float)(G - 1) / 2.0f;
+    const float *conf = p->conf + (uint64_t)q * V;
+    for (int g = 0; g < V; g++) {
+        if (!(conf[g] > 0.0f)) continue;
+        int z = g / (G * G), rem = g % (G * G), y = rem / G, x = rem % G;
+        float rx = ((float)x - gof) * step, ry = ((float)y - gof) * step, rz = ((float)z - gof) * step;
+        f3 pos = {c.x + rx, c.y + ry, c.z + rz};
+        float h[4];
+        t44(pos, p->proj, h);
+        float pw = 1.0f / (h[3] + 0.0000001f);
+        f2 s = {ndc2pix(h[0] * pw, p->W), ndc2pix(h[1] * pw, p->H)};
+        if (!in_pixel(s, px, py)) continue;
+        float m = occ_mag_conf(conf, G, g, S, cf);
+        if (m > 1e-7f) {
+            lanes[n] = g;
+            mags[n] = m;
+            n++;
+        }
+    }
+    return n;
+}
+
 /* ------------------------------------------------------------------------ */
 /* R5: render (forward.cu:146-792), per tile, program order                   */
 /* ------------------------------------------------------------------------ */

@@ -106,3 +106,18 @@ def test_binding_raises_runtime_error_on_a_c_abi_error():
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stderr[-2000:]
     assert "raised: volume_integration: bad layout query (status 1)" in r.stdout
+
+
+def test_exact_restatement_reproduces_the_forward():
+    """The float64 restatement behind the exact-gradient tests computes the
+    oracle's forward images (it is the forward, on the same discrete structure)."""
+    import vi_testlib as tl
+    import exact_lib as ex
+    means, conf, s = tl.custom_scene(P=50, W=48, H=32, seed=5, device="cpu", bg=(0.3, 0.1, 0.6))
+    dc, df = tl.random_grads(s, seed=1, device="cpu")
+    dv = torch.zeros(s.image_height, s.image_width)
+    img, grads, f = ex.exact_grads(means, conf, s, dc, df, dv)
+    np.testing.assert_allclose(img["out_color"], f["out_color"], atol=1e-4)
+    np.testing.assert_allclose(img["out_features"], f["out_features"], atol=1e-4)
+    np.testing.assert_allclose(img["visibility"], f["visibility"], atol=1e-4)
+    assert np.abs(grads["dL_dmeans3D"]).max() > 0 and np.abs(grads["dL_dfeature_table"]).max() > 0

@@ -56,7 +56,7 @@ std::tuple<int, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor> integrate_primit
     const int64_t stencil_genus, const int64_t grid_size, const int64_t max_primitives_per_ray,
     const double occupancy_threshold, const Tensor& bg_color, const int64_t input_feature_dim,
     const int64_t output_feature_dim, const int64_t intermediate_feature_dim, const int64_t hashgrid_levels,
-    const int64_t num_output_channels, const bool debug, const std::vector<double>& hash_bounds) {
+    const int64_t num_output_channels, const bool debug, const std::vector<double>& hash_bounds, const int64_t flags) {
   TORCH_CHECK(means3D.dim() == 2 && means3D.size(1) == 3, "means3D must have shape (P, 3)");
   float hb[6];
   const at::cuda::CUDAGuard guard(means3D.device());
@@ -88,7 +88,7 @@ std::tuple<int, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor> integrate_primit
       (int)grid_size, (int)max_primitives_per_ray, (float)occupancy_threshold, bg.data_ptr<float>(),
       (unsigned)input_feature_dim, (unsigned)output_feature_dim, (unsigned)intermediate_feature_dim,
       (unsigned)hashgrid_levels, (unsigned)num_output_channels, debug ? 1 : 0,
-      at::cuda::getCurrentCUDAStream().stream(), bounds_ptr(hash_bounds, hb)));
+      at::cuda::getCurrentCUDAStream().stream(), bounds_ptr(hash_bounds, hb), (unsigned)flags));
   return {num_rendered, out_color, out_features, visibility, geom, binning, img};
 }
 
@@ -108,7 +108,7 @@ std::tuple<int, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor> integrate_primit
                                  feature_table, resolution, do_hash, primes, feature_offset, linear_weights,
                                  linear_bias, stencil_genus, grid_size, max_primitives_per_ray, occupancy_threshold,
                                  bg_color, input_feature_dim, output_feature_dim, intermediate_feature_dim,
-                                 hashgrid_levels, num_output_channels, debug, {});
+                                 hashgrid_levels, num_output_channels, debug, {}, 0);
 }
 
 std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> integrate_primitives_backward_ex(
@@ -122,9 +122,11 @@ std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> integrate_primitives_backward
     const int64_t max_primitives_per_ray, const double occupancy_threshold, const Tensor& bg_color,
     const int64_t input_feature_dim, const int64_t output_feature_dim, const int64_t hashgrid_levels,
     const int64_t num_output_channels, const int64_t feature_table_size, const int64_t P, const int64_t num_rendered,
-    const bool debug, const std::vector<double>& hash_bounds) {
+    const bool debug, const std::vector<double>& hash_bounds, const int64_t flags, const Tensor& dL_dvisibility) {
   const at::cuda::CUDAGuard guard(means3D.device());
   float hb[6];
+  Tensor gv = dL_dvisibility.numel() ? cuda_f32(dL_dvisibility, "dL_dvisibility") : dL_dvisibility;
+  TORCH_CHECK(!gv.numel() || gv.numel() == image_height * image_width, "dL_dvisibility must be (H, W)");
   Tensor m = cuda_f32(means3D, "means3D"), c = cuda_f32(primitive_confidences, "primitive_confidences");
   Tensor vm = cuda_f32(viewmatrix, "viewmatrix"), pm = cuda_f32(projmatrix, "projmatrix");
   Tensor cp = cuda_f32(cam_pos, "cam_pos"), ft = aligned_table(feature_table);
@@ -152,7 +154,8 @@ std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> integrate_primitives_backward
       lw.data_ptr<float>(), lb.data_ptr<float>(), (int)stencil_genus, (int)grid_size, (int)max_primitives_per_ray,
       (float)occupancy_threshold, bg.data_ptr<float>(), (unsigned)input_feature_dim, (unsigned)output_feature_dim,
       (unsigned)hashgrid_levels, (unsigned)num_output_channels, (uint64_t)feature_table_size, (int)P,
-      (int)num_rendered, debug ? 1 : 0, at::cuda::getCurrentCUDAStream().stream(), bounds_ptr(hash_bounds, hb)));
+      (int)num_rendered, debug ? 1 : 0, at::cuda::getCurrentCUDAStream().stream(), bounds_ptr(hash_bounds, hb),
+      (unsigned)flags, gv.numel() ? gv.data_ptr<float>() : nullptr));
   return {dmeans, dconf, dtable, dW, db};
 }
 
@@ -174,7 +177,8 @@ std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> integrate_primitives_backward
       primitive_scale, viewmatrix, projmatrix, cam_pos, tan_fovx, tan_fovy, image_height, image_width, near_plane,
       max_distance, feature_table, resolution, do_hash, primes, feature_offset, linear_weights, linear_bias,
       stencil_genus, grid_size, max_primitives_per_ray, occupancy_threshold, bg_color, input_feature_dim,
-      output_feature_dim, hashgrid_levels, num_output_channels, feature_table_size, P, num_rendered, debug, {});
+      output_feature_dim, hashgrid_levels, num_output_channels, feature_table_size, P, num_rendered, debug, {}, 0,
+      Tensor());
 }
 
 Tensor mark_visible(Tensor& means3D, Tensor& viewmatrix, Tensor& projmatrix) {
@@ -247,9 +251,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("integrate_primitives", &integrate_primitives, "Integrate Primitives CUDA forward");
   m.def("integrate_primitives_backward", &integrate_primitives_backward, "Integrate Primitives CUDA backward");
   m.def("integrate_primitives_ex", &integrate_primitives_ex,
-        "integrate_primitives with a hashgrid box (31st argument: 6 floats, or [] for the reference's box)");
+        "integrate_primitives plus a hashgrid box (6 floats, or [] for the reference's box) and flags "
+        "(1 = exact gradients)");
   m.def("integrate_primitives_backward_ex", &integrate_primitives_backward_ex,
-        "integrate_primitives_backward with a hashgrid box (38th argument)");
+        "integrate_primitives_backward plus the hashgrid box, flags and dL/dvisibility (empty = none)");
+  m.attr("FLAG_EXACT_GRADIENTS") = (int64_t)VI_FLAG_EXACT_GRADIENTS;
   m.def("mark_visible", &mark_visible, "Mark Visible Primitives CUDA");
   m.def("state_views", &state_views, "Integer state of a forward call in the reference's formats");
   m.def("sort_pairs", &sort_pairs, "Stable radix sort of (uint64 key, uint32 value) pairs");

@@ -172,7 +172,7 @@ BinState bin_layout(char* base, uint64_t R, int tb) {
   return b;
 }
 
-ImgState img_layout(char* base, size_t N, int K, size_t tiles) {
+ImgState img_layout(char* base, size_t N, int K, size_t tiles, bool exact) {
   ImgState m;
   Carver c(base);
   m.ranges = c.take<uint32_t>(2 * tiles);
@@ -181,6 +181,8 @@ ImgState img_layout(char* base, size_t N, int K, size_t tiles) {
   m.contrib_idx = c.take<int32_t>(N * (size_t)K);
   m.delta_t = c.take<float>(N * (size_t)K);
   m.contrib_rec = c.take<uint32_t>(N * (size_t)K);
+  m.trans = exact ? c.take<float>(N * (size_t)K) : nullptr;
+  m.trig = exact ? c.take<uint32_t>(N * (size_t)K) : nullptr;
   m.bytes = c.size();
   return m;
 }
@@ -222,6 +224,7 @@ int make_scene(Scene& sc, int P, const float* means3D, const float* conf, float 
   sc.res = res; sc.do_hash = do_hash; sc.primes = primes; sc.Wl = Wl; sc.bl = bl; sc.bg = bg;
   sc.gx = (unsigned)(W + VI_TILE - 1) / VI_TILE;
   sc.gy = (unsigned)(H + VI_TILE - 1) / VI_TILE;
+  sc.exact = false;
   for (int a = 0; a < 3; a++) {
     if (!hash_bounds) {
       sc.hlo[a] = -1.3f;  // hashgrid.h:225-226
@@ -277,7 +280,7 @@ int forward_impl(
     uint64_t linear_bias_numel, int stencil_genus, int grid_size, int max_primitives_per_ray,
     float occupancy_threshold, const float* bg_color, unsigned input_feature_dim, unsigned output_feature_dim,
     unsigned intermediate_feature_dim, unsigned hashgrid_levels, unsigned num_output_channels, int debug,
-    void* stream, const float* hash_bounds) {
+    void* stream, const float* hash_bounds, unsigned flags) {
   (void)cam_pos;
   (void)occupancy_threshold;  // has no effect in the reference either (forward.cu:118-140 is never called)
   cudaStream_t s = (cudaStream_t)stream;
@@ -291,6 +294,8 @@ int forward_impl(
                       max_primitives_per_ray, bg_color, input_feature_dim, output_feature_dim, hashgrid_levels,
                       num_output_channels, hash_bounds);
   if (rc) return rc;
+  if (flags & ~VI_FLAG_EXACT_GRADIENTS) return fail(VI_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
+  sc.exact = (flags & VI_FLAG_EXACT_GRADIENTS) != 0;
   if (intermediate_feature_dim != hashgrid_levels * input_feature_dim)
     return fail(VI_ERR_INVALID_ARGUMENT,
                 "intermediate_feature_dim=%u must equal hashgrid_levels*input_feature_dim=%u (the reference reads "
@@ -322,11 +327,11 @@ int forward_impl(
   if (!gb) return fail(VI_ERR_ALLOC, "geometry buffer of %zu bytes", g.bytes);
   if ((uintptr_t)gb & 255) return fail(VI_ERR_INVALID_ARGUMENT, "state buffers must be 256-byte aligned");
   g = geom_layout(gb, P, sc.V, sc.O, sc.D);
-  ImgState im = img_layout(nullptr, N, sc.K, tiles);
+  ImgState im = img_layout(nullptr, N, sc.K, tiles, sc.exact);
   char* ib = img_buffer(img_user, im.bytes);
   if (!ib) return fail(VI_ERR_ALLOC, "image buffer of %zu bytes", im.bytes);
   if ((uintptr_t)ib & 255) return fail(VI_ERR_INVALID_ARGUMENT, "state buffers must be 256-byte aligned");
-  im = img_layout(ib, N, sc.K, tiles);
+  im = img_layout(ib, N, sc.K, tiles, sc.exact);
 
   cudaMemsetAsync(g.status, 0, 64 * sizeof(uint32_t), s);
   stage_begin(kStPreprocess, s);
@@ -399,10 +404,10 @@ int backward_impl(
     const float* linear_weights, const float* linear_bias, int stencil_genus, int grid_size,
     int max_primitives_per_ray, float occupancy_threshold, const float* bg_color, unsigned input_feature_dim,
     unsigned output_feature_dim, unsigned hashgrid_levels, unsigned num_output_channels,
-    uint64_t feature_table_size, int P, int num_rendered, int debug, void* stream, const float* hash_bounds) {
+    uint64_t feature_table_size, int P, int num_rendered, int debug, void* stream, const float* hash_bounds,
+    unsigned flags, const float* dL_dvisibility) {
   (void)cam_pos;
   (void)occupancy_threshold;
-  (void)binning_buffer;  // the backward walks per-pixel contributor lists, not tile lists
   cudaStream_t s = (cudaStream_t)stream;
   Scene sc;
   int rc = make_scene(sc, P, means3D, primitive_confidences, primitive_scale, viewmatrix, projmatrix, tan_fovx,
@@ -411,6 +416,8 @@ int backward_impl(
                       max_primitives_per_ray, bg_color, input_feature_dim, output_feature_dim, hashgrid_levels,
                       num_output_channels, hash_bounds);
   if (rc) return rc;
+  if (flags & ~VI_FLAG_EXACT_GRADIENTS) return fail(VI_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
+  sc.exact = (flags & VI_FLAG_EXACT_GRADIENTS) != 0;
   if (feature_table_size < (uint64_t)sc.T * sc.L * sc.F)
     return fail(VI_ERR_INVALID_ARGUMENT, "feature_table_size=%llu < feature_offset*L*F", (unsigned long long)feature_table_size);
   // Zeroed outputs (integrator_impl.cu:573-577).
@@ -430,9 +437,19 @@ int backward_impl(
       ((uintptr_t)dL_dfeature_table) % (size_t)(sc.F >= 4 ? 16 : sc.F * 4) != 0)
     return fail(VI_ERR_INVALID_ARGUMENT, "feature_table and its gradient must be aligned to one entry's vector");
   GeomState g = geom_layout(geom_buffer, P, sc.V, sc.O, sc.D);
-  ImgState im = img_layout(img_buffer, N, sc.K, (size_t)sc.gx * sc.gy);
-  launch_backward(sc, g, im, dL_dout_color, sc.Fout ? dL_dout_features : nullptr, dL_dconfidences,
-                  dL_dfeature_table, dL_dlinear_weights, dL_dlinear_bias, s);
+  ImgState im = img_layout(img_buffer, N, sc.K, (size_t)sc.gx * sc.gy, sc.exact);
+  const uint32_t* point_list = nullptr;
+  if (sc.exact) {
+    // the list index of a composite's trigger resolves to a primitive through the point list
+    if (!binning_buffer) return fail(VI_ERR_INVALID_ARGUMENT, "the exact-gradient backward needs the binning buffer");
+    const int tb = tile_bits((size_t)sc.gx * sc.gy);
+    BinState b = bin_layout(binning_buffer, (uint64_t)num_rendered, tb);
+    // The tile sort runs ceil(bits/8) passes; an odd count leaves the result in the alternate arrays.
+    const bool alt = num_rendered > 1 && (((tb + 7) / 8) & 1);
+    point_list = alt ? b.tvals_alt : b.tvals;
+  }
+  launch_backward(sc, g, im, point_list, dL_dout_color, sc.Fout ? dL_dout_features : nullptr, dL_dvisibility,
+                  dL_dmeans3D, dL_dconfidences, dL_dfeature_table, dL_dlinear_weights, dL_dlinear_bias, s);
   return check(s, debug, "backward", g.status);
 }
 
@@ -456,7 +473,7 @@ extern "C" int vi_integrate_primitives(
                       feature_table, feature_table_numel, resolution, do_hash, primes, feature_offset, linear_weights,
                       linear_weights_numel, linear_bias, linear_bias_numel, stencil_genus, grid_size,
                       max_primitives_per_ray, occupancy_threshold, bg_color, input_feature_dim, output_feature_dim,
-                      intermediate_feature_dim, hashgrid_levels, num_output_channels, debug, stream, nullptr);
+                      intermediate_feature_dim, hashgrid_levels, num_output_channels, debug, stream, nullptr, 0u);
 }
 
 extern "C" int vi_integrate_primitives_ex(
@@ -470,14 +487,15 @@ extern "C" int vi_integrate_primitives_ex(
     uint64_t linear_bias_numel, int stencil_genus, int grid_size, int max_primitives_per_ray,
     float occupancy_threshold, const float* bg_color, unsigned input_feature_dim, unsigned output_feature_dim,
     unsigned intermediate_feature_dim, unsigned hashgrid_levels, unsigned num_output_channels, int debug,
-    void* stream, const float* hash_bounds) {
+    void* stream, const float* hash_bounds, unsigned flags) {
   return forward_impl(geom_buffer, geom_user, binning_buffer, binning_user, img_buffer, img_user, out_color, out_features,
                       visibility_info, num_rendered, P, means3D, primitive_confidences, primitive_scale, viewmatrix,
                       projmatrix, cam_pos, tan_fovx, tan_fovy, image_height, image_width, near_plane, max_distance,
                       feature_table, feature_table_numel, resolution, do_hash, primes, feature_offset, linear_weights,
                       linear_weights_numel, linear_bias, linear_bias_numel, stencil_genus, grid_size,
                       max_primitives_per_ray, occupancy_threshold, bg_color, input_feature_dim, output_feature_dim,
-                      intermediate_feature_dim, hashgrid_levels, num_output_channels, debug, stream, hash_bounds);
+                      intermediate_feature_dim, hashgrid_levels, num_output_channels, debug, stream, hash_bounds,
+                      flags);
 }
 
 extern "C" int vi_integrate_primitives_backward(
@@ -497,7 +515,8 @@ extern "C" int vi_integrate_primitives_backward(
                        image_height, image_width, near_plane, max_distance, feature_table, resolution, do_hash,
                        primes, feature_offset, linear_weights, linear_bias, stencil_genus, grid_size,
                        max_primitives_per_ray, occupancy_threshold, bg_color, input_feature_dim, output_feature_dim,
-                       hashgrid_levels, num_output_channels, feature_table_size, P, num_rendered, debug, stream, nullptr);
+                       hashgrid_levels, num_output_channels, feature_table_size, P, num_rendered, debug, stream, nullptr,
+                       0u, nullptr);
 }
 
 extern "C" int vi_integrate_primitives_backward_ex(
@@ -510,14 +529,16 @@ extern "C" int vi_integrate_primitives_backward_ex(
     const float* linear_weights, const float* linear_bias, int stencil_genus, int grid_size,
     int max_primitives_per_ray, float occupancy_threshold, const float* bg_color, unsigned input_feature_dim,
     unsigned output_feature_dim, unsigned hashgrid_levels, unsigned num_output_channels,
-    uint64_t feature_table_size, int P, int num_rendered, int debug, void* stream, const float* hash_bounds) {
+    uint64_t feature_table_size, int P, int num_rendered, int debug, void* stream, const float* hash_bounds,
+    unsigned flags, const float* dL_dvisibility) {
   return backward_impl(dL_dmeans3D, dL_dconfidences, dL_dfeature_table, dL_dlinear_weights, dL_dlinear_bias,
                        dL_dout_color, dL_dout_features, geom_buffer, binning_buffer, img_buffer, means3D,
                        primitive_confidences, primitive_scale, viewmatrix, projmatrix, cam_pos, tan_fovx, tan_fovy,
                        image_height, image_width, near_plane, max_distance, feature_table, resolution, do_hash,
                        primes, feature_offset, linear_weights, linear_bias, stencil_genus, grid_size,
                        max_primitives_per_ray, occupancy_threshold, bg_color, input_feature_dim, output_feature_dim,
-                       hashgrid_levels, num_output_channels, feature_table_size, P, num_rendered, debug, stream, hash_bounds);
+                       hashgrid_levels, num_output_channels, feature_table_size, P, num_rendered, debug, stream, hash_bounds,
+                       flags, dL_dvisibility);
 }
 
 extern "C" int vi_mark_visible(int P, const float* means3D, const float* viewmatrix, const float* projmatrix,
@@ -562,7 +583,7 @@ extern "C" int vi_get_state_layout(int P, int64_t num_rendered, int image_height
   GeomState g = geom_layout(nullptr, P, V, O, 0);
   const int tb = tile_bits(tiles);
   BinState b = bin_layout(nullptr, (uint64_t)num_rendered, tb);
-  ImgState m = img_layout(nullptr, N, max_primitives_per_ray, tiles);
+  ImgState m = img_layout(nullptr, N, max_primitives_per_ray, tiles, false);
   out->geom_bytes = g.bytes;
   out->binning_bytes = b.bytes;
   out->img_bytes = m.bytes;

@@ -185,6 +185,132 @@ __global__ void __launch_bounds__(256) backward_pixel_kernel(Scene sc, GeomState
   }
 }
 
+// Exact-gradient mode, per pixel: the derivative of the forward's compositing
+// (forward.cu:649-785 as this build computes it) with respect to each
+// contribution's activated properties and delta t.  With T_i the
+// transmittance before contribution i and a_i its alpha, the colour is
+// C = sum_i T_i a_i c_i + T_n bg (clamped to [0, 1]) and
+//   dC/dc_i = T_i a_i,   dC/da_i = T_i (c_i - A_i),
+// where A_i, the colour behind contribution i, follows A <- a c + (1 - a) A
+// from A = bg back to front; features likewise from 0, visibility 1 - T_n with
+// dT_n/da_i = -T_i prod_{j>i} (1 - a_j).  A first front-to-back pass recovers
+// the unclamped colour for the clamp.  dL/d(delta t) moves the depths of the
+// composited primitive and of the one whose arrival composited it; depth is
+// the view-space z of the centre, so dL/dmeans3D gains dL/ddepth * (m2, m6, m10).
+template <int OMAX>
+__global__ void __launch_bounds__(256) backward_pixel_exact_kernel(Scene sc, GeomState g, ImgState im,
+                                                                  const uint32_t* __restrict__ point_list,
+                                                                  const float* __restrict__ dL_dcolor,
+                                                                  const float* __restrict__ dL_dfeat,
+                                                                  const float* __restrict__ dL_dvis,
+                                                                  float* __restrict__ dmeans) {
+  const size_t N = (size_t)sc.W * sc.H;
+  const size_t pix = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (pix >= N) return;
+  const int K = sc.K;
+  const int nc = min(im.n_contrib[pix], K);
+  if (nc <= 0) return;
+  const int O = sc.O, B = O - 1, Fout = sc.Fout, V = sc.V;
+  const uint32_t* crec = im.contrib_rec + pix * K;
+  const float* cdt = im.delta_t + pix * K;
+  const float* ctr = im.trans + pix * K;
+  const uint32_t* ctg = im.trig + pix * K;
+  auto load_props = [&](uint32_t rec, float* props) {
+    const float4* src = reinterpret_cast<const float4*>(g.rec_props + (size_t)rec * OMAX);
+#pragma unroll
+    for (int o4 = 0; o4 < OMAX / 4; o4++) {
+      const float4 v = src[o4];
+      props[4 * o4] = v.x; props[4 * o4 + 1] = v.y; props[4 * o4 + 2] = v.z; props[4 * o4 + 3] = v.w;
+    }
+  };
+  auto alpha_of = [&](float sigma, float dt, float& e) {
+    e = expf(-sigma * dt);
+    return fminf(fmaxf(1.0f - e, 0.0f), 1.0f);
+  };
+  // Pass 1: the unclamped colour (the final clamp's derivative is 0 outside (0, 1)).
+  float C[3] = {0.0f, 0.0f, 0.0f};
+  for (int k = 0; k < nc; k++) {
+    float props[OMAX], e;
+    load_props(crec[k] & ~kBwdDiffers, props);
+    float sig = 0.0f;
+#pragma unroll
+    for (int o = 0; o < OMAX; o++)
+      if (o == B) sig = props[o];
+    const float a = alpha_of(sig, cdt[k], e), w = ctr[k] * a;
+#pragma unroll
+    for (int c = 0; c < 3; c++) C[c] += w * props[c];
+  }
+  const float Tn = im.final_T[pix];
+  float gC[3], A[OMAX - 1];
+#pragma unroll
+  for (int c = 0; c < 3; c++) {
+    const float x = C[c] + Tn * sc.bg[c];
+    gC[c] = (x > 0.0f && x < 1.0f) ? dL_dcolor[c * N + pix] : 0.0f;
+    A[c] = sc.bg[c];
+  }
+  float gF[OMAX - 4];
+#pragma unroll
+  for (int f = 0; f < OMAX - 4; f++) {
+    gF[f] = (f < Fout && dL_dfeat) ? dL_dfeat[f * N + pix] : 0.0f;
+    A[3 + f] = 0.0f;
+  }
+  const float gV = dL_dvis ? dL_dvis[pix] : 0.0f;
+  float Vp = 1.0f;  // prod_{j>i} (1 - a_j)
+  const float vz0 = sc.view[2], vz1 = sc.view[6], vz2 = sc.view[10];
+  // Pass 2, back to front.
+  for (int k = nc - 1; k >= 0; k--) {
+    const uint32_t rec = crec[k] & ~kBwdDiffers;
+    float props[OMAX], e;
+    load_props(rec, props);
+    float sig = 0.0f;
+#pragma unroll
+    for (int o = 0; o < OMAX; o++)
+      if (o == B) sig = props[o];
+    const float dt = cdt[k], T = ctr[k];
+    const float a = alpha_of(sig, dt, e), Ta = T * a;
+    float dLda = gV * T * Vp, dpre[OMAX];
+#pragma unroll
+    for (int d = 0; d < OMAX - 1; d++) {
+      if (d < B) {
+        const float y = props[d], g = d < 3 ? gC[d] : gF[d - 3];
+        dLda += g * T * (y - A[d]);
+        dpre[d] = g * Ta * y * (1.0f - y);  // sigmoid
+      }
+    }
+    // a = 1 - exp(-sigma dt): da/dsigma = dt e, da/ddt = sigma e; sigma = exp(pre)
+    const bool inside = a > 0.0f && a < 1.0f;
+    const float dLds = inside ? dLda * dt * e : 0.0f;
+    const float dLddt = inside ? dLda * sig * e : 0.0f;
+#pragma unroll
+    for (int o = 0; o < OMAX; o++) {
+      if (o == B) dpre[o] = dLds * sig;
+      else if (o > B) dpre[o] = 0.0f;
+    }
+    float4* dst = reinterpret_cast<float4*>(g.rec_dpre + (size_t)rec * OMAX);
+#pragma unroll
+    for (int o4 = 0; o4 < OMAX / 4; o4++) dst[o4] = make_float4(dpre[4 * o4], dpre[4 * o4 + 1], dpre[4 * o4 + 2], dpre[4 * o4 + 3]);
+    g.rec_pix[rec] = (uint32_t)pix + 1u;
+    // delta t = depth(trigger) - depth(this primitive), or max_distance - depth
+    if (dLddt != 0.0f) {
+      const uint32_t q = rec / V;
+      atomicAdd(dmeans + 3 * q, -dLddt * vz0);
+      atomicAdd(dmeans + 3 * q + 1, -dLddt * vz1);
+      atomicAdd(dmeans + 3 * q + 2, -dLddt * vz2);
+      const uint32_t tg = ctg[k];
+      if (tg != 0xffffffffu) {
+        const uint32_t qt = point_list[tg];
+        atomicAdd(dmeans + 3 * qt, dLddt * vz0);
+        atomicAdd(dmeans + 3 * qt + 1, dLddt * vz1);
+        atomicAdd(dmeans + 3 * qt + 2, dLddt * vz2);
+      }
+    }
+#pragma unroll
+    for (int d = 0; d < OMAX - 1; d++)
+      if (d < B) A[d] = a * props[d] + (1.0f - a) * A[d];
+    Vp *= 1.0f - a;
+  }
+}
+
 template <int F>
 __device__ __forceinline__ void atomic_vec(float* p, const float* x) {
   if constexpr (F == 2) {
@@ -254,6 +380,49 @@ __device__ __forceinline__ void gather_scatter_level(const LevelCorners& c, cons
   }
 }
 
+// gather_scatter_level plus the derivative of the interpolation with respect to
+// the cell fractions: dt3[a] += sum_f A[f] * sum_k table_k,f * dw_k/dt_a, where
+// w_k = wx wy wz and each factor is 1 - t or t (exact-gradient mode).
+template <int F, bool POW2>
+__device__ __forceinline__ void gather_scatter_grad_level(const LevelCorners& c, const float* __restrict__ lvl,
+                                                          float* __restrict__ dst, uint32_t stride, uint32_t T,
+                                                          uint32_t Tmask, bool doA, const float* A, float* acc,
+                                                          float* dt3) {
+  const uint32_t hxy[4] = {c.hsh ? c.ix0 ^ c.iy0 : c.ix0 + c.iy0, c.hsh ? c.ix0 ^ c.iy1 : c.ix0 + c.iy1,
+                           c.hsh ? c.ix1 ^ c.iy0 : c.ix1 + c.iy0, c.hsh ? c.ix1 ^ c.iy1 : c.ix1 + c.iy1};
+#pragma unroll
+  for (int k = 0; k < 8; k++) {
+    if ((c.mask >> k) & 1u) {
+      const uint32_t z = (k & 1) ? c.iz1 : c.iz0;
+      uint32_t e;
+      if (c.hsh) {
+        const uint32_t h = hxy[k >> 1] ^ z;
+        e = POW2 ? (h & Tmask) : (h % T);
+      } else {
+        e = hxy[k >> 1] + z;
+      }
+      const float wx = (k & 4) ? c.wx1 : c.wx0, wy = (k & 2) ? c.wy1 : c.wy0, wz = (k & 1) ? c.wz1 : c.wz0;
+      const float w = wx * wy * wz;
+      const FVec<F> v = load_feat<F>(lvl + (size_t)e * stride);
+      float av = 0.0f;
+#pragma unroll
+      for (int f = 0; f < F; f++) {
+        acc[f] += v.v[f] * w;
+        av += A[f] * v.v[f];
+      }
+      dt3[0] += av * ((k & 4) ? 1.0f : -1.0f) * wy * wz;
+      dt3[1] += av * ((k & 2) ? 1.0f : -1.0f) * wx * wz;
+      dt3[2] += av * ((k & 1) ? 1.0f : -1.0f) * wx * wy;
+      if (doA) {
+        float x[F];
+#pragma unroll
+        for (int f = 0; f < F; f++) x[f] = A[f] * w;
+        atomic_vec<F>(dst + (size_t)e * stride, x);
+      }
+    }
+  }
+}
+
 // The scatter half of gather_scatter_level: A[f] * (corner weight) into the
 // table gradient at each corner of one (position, level) query.
 template <int F, bool POW2>
@@ -291,8 +460,13 @@ __device__ __forceinline__ void scatter_level(const LevelCorners& c, float* __re
 // corners, so conf*vA and E are summed per position class; the hashgrid gather
 // (for phi) and scatter (for the table gradient) then run once per (class,
 // level), spread over the warp's lanes.
-template <int F, int OMAX>
-__global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene sc, GeomState g, float* __restrict__ dconf,
+// EXACT: the exact-gradient mode (see backward_pixel_exact_kernel): grid points
+// join records by the forward projection, dconf = mag (W phi) . dpre for the
+// grid points that form the record, the table coefficient of a class is
+// W^T (sum of E), and dL/dmeans3D gains the hashgrid's spatial derivative.
+template <int F, int OMAX, bool EXACT>
+__global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene sc, GeomState g, float* __restrict__ dmeans,
+                                                                      float* __restrict__ dconf,
                                                                       float* __restrict__ dtable, float* __restrict__ dW,
                                                                       float* __restrict__ db) {
   extern __shared__ float4 smem4[];
@@ -363,7 +537,9 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
     const float conf = act ? sc.conf[s0 + lane] : 0.0f;
     const float3 c = make_float3(sc.means[3 * q], sc.means[3 * q + 1], sc.means[3 * q + 2]);
     const float3 pos = grid_pos_rel(c, gpt.rel, sc.step);
-    const float2 sb = project(pos, sc.proj, sc.W, sc.H, false);
+    // the reference's backward recomputes screen positions with 1/w
+    // (backward.cu:325); the exact mode follows the forward's 1/(w + 1e-7)
+    const float2 sb = project(pos, sc.proj, sc.W, sc.H, EXACT);
     const int bx = pix_coord(sb.x), by = pix_coord(sb.y);
     const int bpix = (act && bx >= 0 && bx < sc.W && by >= 0 && by < sc.H) ? by * sc.W + bx : -1;
     const uint32_t posm = __ballot_sync(0xffffffffu, act && conf > 0.0f);
@@ -400,7 +576,23 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
         }
       }
     };
-    if (st.S == 3) {
+    if (EXACT) {
+      // Only the grid points that form a record carry gradient (E rows).
+      int myrec = -1;
+      uint32_t m = cm;
+      while (m) {
+        const int j = __ffs(m) - 1;
+        m &= m - 1;
+        const int ppix = (int)__shfl_sync(0xffffffffu, rp, j) - 1;
+        if (bpix == ppix) myrec = j;
+        if ((int)lane < O) dbacc += S_s[j * OMAX + lane];
+      }
+      if (myrec >= 0 && wE != 0.0f) {
+        hasE = true;
+#pragma unroll
+        for (int o = 0; o < OMAX; o++) el_s[lane * OMAX + o] = fmul(wE, S_s[myrec * OMAX + o]);
+      }
+    } else if (st.S == 3) {
       // 3-tap stencil: an axis adds 1/2 to record p exactly when one of the two
       // neighbours along it lies in p's pixel (backward.cu:654-689), so a grid
       // point only meets the records of its neighbours' pixels.  myrec = the
@@ -480,7 +672,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
     // With the forward's class features (phi_cache) the classes are those of
     // all grid points, as in the feature stage; otherwise those of the
     // gathering lanes only.
-    const uint32_t cb = g.cls_base[q];
+    const uint32_t cb = EXACT ? kNoCache : g.cls_base[q];  // the exact mode gathers (spatial derivative)
     const bool cached = cb != kNoCache;
     const bool member = cached ? act : gather;
     const float3 nrm = hash_norm(pos, sc.hlo, sc.hext);
@@ -540,10 +732,11 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
     // gradient, and gather phi unless the forward cached it.  Lanes of one
     // level that hit the same table entry share one request.
     const LevelWalk it(pc.U, L);
+    float dpos[3] = {0.0f, 0.0f, 0.0f};
     for (int l0 = 0; l0 < L; l0 += it.per) {
       if (!it.valid(l0)) continue;
       const int l = it.level(l0), u = it.u;
-      const bool doA = (mem_s[u] & amask) != 0u;
+      const bool doA = (mem_s[u] & (EXACT ? emask : amask)) != 0u;
       if (cached && !doA) continue;
       const float4 n4 = npos_s[u];
       const LevelCorners lc = level_corners(make_float3(n4.x, n4.y, n4.z), res_s[l], resf_s[l], hash_s[l] != 0,
@@ -556,7 +749,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
         float sum = 0.0f;
         if (doA) {
 #pragma unroll
-          for (int o = 0; o < OMAX; o++) sum += W_s[o * DP + l * F + f] * S_s[u * OMAX + o];
+          for (int o = 0; o < OMAX; o++) sum += W_s[o * DP + l * F + f] * (EXACT ? Es_s : S_s)[u * OMAX + o];
         }
         A[f] = sum;
       }
@@ -569,12 +762,36 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
           scatter_level<F, false>(lc, dst, stride, sc.T, sc.Tmask, A);
         continue;
       }
-      if (sc.Tmask)
+      if (EXACT) {
+        float dt3[3] = {0.0f, 0.0f, 0.0f};  // sum_f A_f dphi_f / dt per axis
+        if (sc.Tmask)
+          gather_scatter_grad_level<F, true>(lc, lvl, dst, stride, sc.T, sc.Tmask, doA, A, acc, dt3);
+        else
+          gather_scatter_grad_level<F, false>(lc, lvl, dst, stride, sc.T, sc.Tmask, doA, A, acc, dt3);
+        // t = frac(n * res), n = clamp((p - lo) / ext): dt/dp = res / ext where not clamped
+        const float r = resf_s[l];
+        if (n4.x > 0.0f && n4.x < 1.0f) dpos[0] += dt3[0] * __fdiv_rn(r, sc.hext[0]);
+        if (n4.y > 0.0f && n4.y < 1.0f) dpos[1] += dt3[1] * __fdiv_rn(r, sc.hext[1]);
+        if (n4.z > 0.0f && n4.z < 1.0f) dpos[2] += dt3[2] * __fdiv_rn(r, sc.hext[2]);
+      } else if (sc.Tmask) {
         gather_scatter_level<F, true>(lc, lvl, dst, stride, sc.T, sc.Tmask, doA, A, acc);
-      else
+      } else {
         gather_scatter_level<F, false>(lc, lvl, dst, stride, sc.T, sc.Tmask, doA, A, acc);
+      }
 #pragma unroll
       for (int f = 0; f < F; f++) phi_s[u * DP + l * F + f] = acc[f];
+    }
+    if (EXACT) {
+      // grid point positions are the centre plus fixed offsets: dL/dmeans3D += sum
+#pragma unroll
+      for (int a = 0; a < 3; a++)
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) dpos[a] += __shfl_xor_sync(0xffffffffu, dpos[a], off);
+      if (lane == 0 && (dpos[0] != 0.0f || dpos[1] != 0.0f || dpos[2] != 0.0f)) {
+        dmeans[3 * q] += dpos[0];  // one warp per primitive; the per-pixel kernel's atomics finished
+        dmeans[3 * q + 1] += dpos[1];
+        dmeans[3 * q + 2] += dpos[2];
+      }
     }
     __syncwarp();
     // W phi per class (into cv_s, free now).
@@ -583,7 +800,17 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
     __syncwarp();
     if (act) {
       float dX = 0.0f;
-      if (gather) {
+      if (EXACT) {
+        // d pre / d conf_g = mag_g (W phi_g) on the record of g's pixel; E_g = conf_g mag_g dpre
+        if (hasE) {
+          const float* mr = mlp_s + pc.cls * OMAX;
+          const float* er = el_s + lane * OMAX;
+          float s = 0.0f;
+#pragma unroll
+          for (int o = 0; o < OMAX; o++) s += mr[o] * er[o];
+          dX = __fdiv_rn(s, conf);
+        }
+      } else if (gather) {
         const float* mr = mlp_s + pc.cls * OMAX;
 #pragma unroll
         for (int o = 0; o < OMAX / 2; o++) dX += v[2 * o] * mr[2 * o] + v[2 * o + 1] * mr[2 * o + 1];
@@ -635,23 +862,25 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
 }
 
 template <int F, int OMAX>
-void launch_prim_t(const Scene& sc, GeomState& g, float* dconf, float* dtable, float* dW, float* db, cudaStream_t s) {
+void launch_prim_t(const Scene& sc, GeomState& g, float* dmeans, float* dconf, float* dtable, float* dW, float* db,
+                   cudaStream_t s) {
   const int D = sc.L * F;
   size_t smem = sizeof(float) * (bwd_head_floats(D, sc.L, OMAX) + kBwdWarps * bwd_warp_floats(D, OMAX));
-  auto k = backward_prim_kernel<F, OMAX>;
+  auto k = sc.exact ? backward_prim_kernel<F, OMAX, true> : backward_prim_kernel<F, OMAX, false>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   cudaMemsetAsync(g.status + 5, 0, sizeof(uint32_t), s);
   int blocks = (sc.P + kBwdWarps - 1) / kBwdWarps;
   blocks = blocks < 148 * 10 ? blocks : 148 * 10;
   if (blocks < 1) blocks = 1;
-  k<<<blocks, kBwdWarps * 32, smem, s>>>(sc, g, dconf, dtable, dW, db);
+  k<<<blocks, kBwdWarps * 32, smem, s>>>(sc, g, dmeans, dconf, dtable, dW, db);
   note_launches(1);
 }
 
 }  // namespace
 
-void launch_backward(const Scene& sc, GeomState& g, const ImgState& im, const float* dL_dcolor, const float* dL_dfeat,
-                     float* dconf, float* dtable, float* dW, float* db, cudaStream_t s) {
+void launch_backward(const Scene& sc, GeomState& g, const ImgState& im, const uint32_t* point_list,
+                     const float* dL_dcolor, const float* dL_dfeat, const float* dL_dvis, float* dmeans, float* dconf,
+                     float* dtable, float* dW, float* db, cudaStream_t s) {
   const size_t N = (size_t)sc.W * sc.H;
   cudaMemsetAsync(g.rec_pix, 0, (size_t)sc.P * sc.V * sizeof(uint32_t), s);
   const bool o16 = sc.O > 8;
@@ -659,18 +888,24 @@ void launch_backward(const Scene& sc, GeomState& g, const ImgState& im, const fl
   if (N > 0) {
     note_launches(1);
     const unsigned blocks = (unsigned)((N + 255) / 256);
-    if (o16)
+    if (sc.exact) {
+      if (o16)
+        backward_pixel_exact_kernel<16><<<blocks, 256, 0, s>>>(sc, g, im, point_list, dL_dcolor, dL_dfeat, dL_dvis, dmeans);
+      else
+        backward_pixel_exact_kernel<8><<<blocks, 256, 0, s>>>(sc, g, im, point_list, dL_dcolor, dL_dfeat, dL_dvis, dmeans);
+    } else if (o16) {
       backward_pixel_kernel<16><<<blocks, 256, 0, s>>>(sc, g, im, dL_dcolor, dL_dfeat);
-    else
+    } else {
       backward_pixel_kernel<8><<<blocks, 256, 0, s>>>(sc, g, im, dL_dcolor, dL_dfeat);
+    }
   }
   stage_end(kStBwdPixel, s);
   stage_begin(kStBwdPrim, s);
   switch (sc.F) {
-    case 1: o16 ? launch_prim_t<1, 16>(sc, g, dconf, dtable, dW, db, s) : launch_prim_t<1, 8>(sc, g, dconf, dtable, dW, db, s); break;
-    case 2: o16 ? launch_prim_t<2, 16>(sc, g, dconf, dtable, dW, db, s) : launch_prim_t<2, 8>(sc, g, dconf, dtable, dW, db, s); break;
-    case 4: o16 ? launch_prim_t<4, 16>(sc, g, dconf, dtable, dW, db, s) : launch_prim_t<4, 8>(sc, g, dconf, dtable, dW, db, s); break;
-    case 8: o16 ? launch_prim_t<8, 16>(sc, g, dconf, dtable, dW, db, s) : launch_prim_t<8, 8>(sc, g, dconf, dtable, dW, db, s); break;
+    case 1: o16 ? launch_prim_t<1, 16>(sc, g, dmeans, dconf, dtable, dW, db, s) : launch_prim_t<1, 8>(sc, g, dmeans, dconf, dtable, dW, db, s); break;
+    case 2: o16 ? launch_prim_t<2, 16>(sc, g, dmeans, dconf, dtable, dW, db, s) : launch_prim_t<2, 8>(sc, g, dmeans, dconf, dtable, dW, db, s); break;
+    case 4: o16 ? launch_prim_t<4, 16>(sc, g, dmeans, dconf, dtable, dW, db, s) : launch_prim_t<4, 8>(sc, g, dmeans, dconf, dtable, dW, db, s); break;
+    case 8: o16 ? launch_prim_t<8, 16>(sc, g, dmeans, dconf, dtable, dW, db, s) : launch_prim_t<8, 8>(sc, g, dmeans, dconf, dtable, dW, db, s); break;
     default: break;
   }
   stage_end(kStBwdPrim, s);

@@ -97,9 +97,12 @@ struct ImgState {
   int32_t* contrib_idx;   // [N*K] index into the sorted overlap list
   float* delta_t;         // [N*K]
   uint32_t* contrib_rec;  // [N*K] record slot of the contribution | kBwdDiffers of its primitive
+  // Exact-gradient mode only (null otherwise):
+  float* trans;           // [N*K] transmittance before the contribution
+  uint32_t* trig;         // [N*K] list index of the entry whose arrival composited it, ~0 = max_distance
   size_t bytes;
 };
-ImgState img_layout(char* base, size_t N, int K, size_t tiles);
+ImgState img_layout(char* base, size_t N, int K, size_t tiles, bool exact);
 
 // ---------------------------------------------------------------------------
 // Per-call constants.
@@ -122,6 +125,7 @@ struct Scene {
   uint64_t table_numel;
   unsigned gx, gy;
   float hlo[3], hext[3];  // hashgrid box: lower corner and extent per axis (reference: -1.3, 2.6)
+  bool exact;             // exact-gradient mode (VI_FLAG_EXACT_GRADIENTS)
 };
 
 void launch_preprocess(const Scene& sc, GeomState& g, cudaStream_t s);
@@ -133,7 +137,8 @@ void launch_mark_visible(int P, const float* means, const float* view, bool* pre
 void launch_features(const Scene& sc, GeomState& g, cudaStream_t s);
 void launch_render(const Scene& sc, const GeomState& g, const uint32_t* point_list, ImgState& im,
                    float* out_color, float* out_feat, float* vis, cudaStream_t s);
-void launch_backward(const Scene& sc, GeomState& g, const ImgState& im, const float* dL_dcolor,
-                     const float* dL_dfeat, float* dconf, float* dtable, float* dW, float* db, cudaStream_t s);
+void launch_backward(const Scene& sc, GeomState& g, const ImgState& im, const uint32_t* point_list,
+                     const float* dL_dcolor, const float* dL_dfeat, const float* dL_dvis, float* dmeans, float* dconf,
+                     float* dtable, float* dW, float* db, cudaStream_t s);
 
 }  // namespace vi

@@ -32,7 +32,8 @@ __global__ void __launch_bounds__(VI_TILE_PIX) render_kernel(Scene sc, const uin
                                                             int32_t* __restrict__ n_contrib,
                                                             int32_t* __restrict__ contrib_idx,
                                                             float* __restrict__ delta_t,
-                                                            uint32_t* __restrict__ contrib_rec) {
+                                                            uint32_t* __restrict__ contrib_rec,
+                                                            float* __restrict__ trans, uint32_t* __restrict__ trig) {
   __shared__ unsigned long long mask[VI_TILE_PIX];
   __shared__ uint8_t slot[VI_TILE_PIX * kBatch];
   __shared__ uint32_t ent_rec[kBatch];
@@ -60,7 +61,9 @@ __global__ void __launch_bounds__(VI_TILE_PIX) render_kernel(Scene sc, const uin
   const uint32_t r0 = ranges[2 * tile], r1 = ranges[2 * tile + 1];
   const uint32_t klo = tile << 8;
 
-  auto composite = [&](float dt) {
+  // trigger: list index of the entry whose arrival composites the pending one,
+  // ~0 for the final composite against max_distance (kept for the exact backward)
+  auto composite = [&](float dt, uint32_t trigger) {
     const float* pp = rec_props + (size_t)pend_rec * OMAX;
     float alpha = 1.0f - expf(-pp[O - 1] * dt);
     alpha = fminf(fmaxf(alpha, 0.0f), 1.0f);
@@ -76,6 +79,10 @@ __global__ void __launch_bounds__(VI_TILE_PIX) render_kernel(Scene sc, const uin
     contrib_idx[w] = (int32_t)pend_gidx;
     delta_t[w] = dt;
     contrib_rec[w] = pend_rec | pend_flag;  // the backward's recompute flag rides in bit 31
+    if (trans) {
+      trans[w] = T_pend;
+      trig[w] = trigger;
+    }
     cnt++;
   };
 
@@ -122,7 +129,7 @@ __global__ void __launch_bounds__(VI_TILE_PIX) render_kernel(Scene sc, const uin
         const float depth = ent_depth[e];
         if (has_p) {
           const float dt = fmaxf(0.0f, depth - pend_depth);
-          if (dt > 1e-5f && cnt < K) composite(dt);
+          if (dt > 1e-5f && cnt < K) composite(dt, base + e);
         }
         if (T >= 1e-4f && cnt < K) {
           pend_rec = rec;
@@ -143,7 +150,7 @@ __global__ void __launch_bounds__(VI_TILE_PIX) render_kernel(Scene sc, const uin
   if (!inside) return;
   if (has_p && T >= 1e-4f && cnt < K) {
     const float dt = fmaxf(0.0f, sc.max_distance - pend_depth);
-    if (dt > 1e-5f) composite(dt);
+    if (dt > 1e-5f) composite(dt, 0xffffffffu);
   }
   const size_t N = (size_t)sc.W * sc.H;
   out_color[pix] = fminf(fmaxf(C0 + T * sc.bg[0], 0.0f), 1.0f);
@@ -167,11 +174,11 @@ void launch_render(const Scene& sc, const GeomState& g, const uint32_t* point_li
   if (sc.O > 8)
     render_kernel<16><<<tiles, VI_TILE_PIX, 0, s>>>(sc, point_list, im.ranges, g.depths, g.rec_cnt, g.rec_key,
                                                     g.rec_props, out_color, out_feat, vis, im.final_T, im.n_contrib,
-                                                    im.contrib_idx, im.delta_t, im.contrib_rec);
+                                                    im.contrib_idx, im.delta_t, im.contrib_rec, im.trans, im.trig);
   else
     render_kernel<8><<<tiles, VI_TILE_PIX, 0, s>>>(sc, point_list, im.ranges, g.depths, g.rec_cnt, g.rec_key,
                                                    g.rec_props, out_color, out_feat, vis, im.final_T, im.n_contrib,
-                                                   im.contrib_idx, im.delta_t, im.contrib_rec);
+                                                   im.contrib_idx, im.delta_t, im.contrib_rec, im.trans, im.trig);
 }
 
 }  // namespace vi

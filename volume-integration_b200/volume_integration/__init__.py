@@ -63,6 +63,11 @@ class IntegrationSettings:
     # at [-1.3, 1.3]^3, hashgrid.h:23-24): (lo_x, lo_y, lo_z, hi_x, hi_y, hi_z)
     # of the box positions are normalised to, or None for the reference's box.
     hash_bounds: Optional[Sequence[float]] = None
+    # Extension: when True the backward is the derivative of the forward
+    # (including dL/dmeans3D and dL/dvisibility_info) instead of the reference's
+    # formula, which is not (no transmittance factor, another occupancy, no
+    # delta-t terms).  Off by default: the reference's gradients.
+    exact_gradients: bool = False
 
 
 def _flat_confidences(conf, P, G):
@@ -89,6 +94,10 @@ def _hash_bounds(s):
     if len(vals) != 6:
         raise ValueError(f"hash_bounds needs 6 values (lo xyz, hi xyz), got {len(vals)}")
     return vals
+
+
+def _flags(s):
+    return int(_C.FLAG_EXACT_GRADIENTS) if getattr(s, "exact_gradients", False) else 0
 
 
 class _IntegratePrimitives(Function):
@@ -124,11 +133,11 @@ class _IntegratePrimitives(Function):
                 s.max_primitives_per_ray, s.occupancy_threshold, bg_color, s.input_feature_dim,
                 s.output_feature_dim, s.intermediate_feature_dim, s.hashgrid_levels, s.num_output_channels,
                 s.debug)
-        hb = _hash_bounds(s)
-        if hb is None:
+        hb, flags = _hash_bounds(s), _flags(s)
+        if hb is None and not flags:
             res = _C.integrate_primitives(*args)
         else:
-            res = _C.integrate_primitives_ex(*args, hb)
+            res = _C.integrate_primitives_ex(*args, hb or [], flags)
         num_rendered, out_color, out_features, visibility_info, geom, binning, img = res
 
         ctx.save_for_backward(means3D, conf_flat, feature_table, linear_weights, linear_bias, viewmatrix,
@@ -154,11 +163,13 @@ class _IntegratePrimitives(Function):
                 s.max_primitives_per_ray, s.occupancy_threshold, bg_color, s.input_feature_dim,
                 s.output_feature_dim, s.hashgrid_levels, s.num_output_channels, feature_table.numel(),
                 means3D.shape[0], ctx.num_rendered, s.debug)
-        hb = _hash_bounds(s)
-        if hb is None:
+        hb, flags = _hash_bounds(s), _flags(s)
+        if hb is None and not flags:
             dmeans, dconf, dtable, dW, db = _C.integrate_primitives_backward(*args)
         else:
-            dmeans, dconf, dtable, dW, db = _C.integrate_primitives_backward_ex(*args, hb)
+            gv = grad_out_visibility if (flags and grad_out_visibility is not None) else torch.empty(0)
+            dmeans, dconf, dtable, dW, db = _C.integrate_primitives_backward_ex(*args, hb or [], flags,
+                                                                                gv.contiguous())
         if ctx.original_confidences_shape is not None:
             dconf = dconf.view(ctx.original_confidences_shape)
         return (dmeans if needs[0] else None, dconf if needs[1] else None, dtable if needs[2] else None,
