@@ -19,9 +19,12 @@
 //       dW, db      += dpre_p (x) in_p, dpre_p                          (backward.cu:621-641)
 //     where g' is the stencil magnitude of "neighbour's screen point lies in
 //     pixel p" (backward.cu:644-689).  The table scatter is linear in dIn, so
-//     each grid point scatters once per level and corner instead of once per
-//     pixel, and lanes hitting the same entry are reduced inside the warp before
-//     one vector atomic.  dW/db are reduced per CTA before global atomics.
+//     each position class scatters once per level and corner instead of once
+//     per pixel and grid point; its features come from the feature stage's
+//     cache.  dW/db are reduced per CTA before global atomics.
+//
+// With the exact-gradient flag both kernels compute the derivative of the
+// forward instead (backward_pixel_exact_kernel, backward_prim_kernel<.., true>).
 #include <cuda_runtime.h>
 
 #include <cstdint>

@@ -114,9 +114,6 @@ __device__ __forceinline__ void level_setup_nf(float3 n, float rf, int3& b, floa
   floor_small(pz, b.z, fz);
   t = make_float3(fsub(px, fx), fsub(py, fy), fsub(pz, fz));
 }
-__device__ __forceinline__ void level_setup_n(float3 n, int res, int3& b, float3& t) {
-  level_setup_nf(n, (float)res, b, t);
-}
 
 __device__ __forceinline__ void level_setup(float3 pos, const float* lo, const float* ext, int res, int3& b, float3& t) {
   float3 n = hash_norm(pos, lo, ext);
@@ -142,14 +139,5 @@ __device__ __forceinline__ int corner_entry(int cx, int cy, int cz, int res, boo
 
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
 
-// Shared per-call constants, passed by value to every kernel.
-struct HashParams {
-  const float* __restrict__ table;
-  const int* __restrict__ res;
-  const int* __restrict__ do_hash;
-  const int* __restrict__ primes;
-  uint32_t T, Tmask;
-  int L, F;
-};
 
 }  // namespace vi

@@ -56,7 +56,7 @@ struct GeomState {
   uint32_t* offsets;         // [P] exclusive overlap offsets in depth order
   uint32_t* block_sums;      // [scan blocks]
   uint32_t* rec_cnt;         // [P] record count | kBwdDiffers
-  uint32_t* rec_key;         // [P*V] tile*256 + pixel-in-tile, sorted per primitive
+  uint32_t* rec_key;         // [P*V] tile*256 + pixel-in-tile, grouped by tile (ascending) per primitive
   float* rec_props;          // [P*V*O] activated colour, features, density per record
   uint32_t* rec_pix;         // [P*V] pixel + 1 of a contributing record, 0 otherwise (backward)
   float* rec_dpre;           // [P*V*O] dL/d(pre-activation) per contributing record

@@ -156,19 +156,6 @@ __device__ __forceinline__ LevelCorners level_corners(float3 nrm, int res, float
   return c;
 }
 
-// Table entry and trilinear weight ((wx * wy) * wz, hashgrid.h:253) of corner k.
-__device__ __forceinline__ uint32_t corner_index(const LevelCorners& c, int k, uint32_t T, uint32_t Tmask) {
-  const uint32_t x = (k & 4) ? c.ix1 : c.ix0, y = (k & 2) ? c.iy1 : c.iy0, z = (k & 1) ? c.iz1 : c.iz0;
-  if (c.hsh) {
-    const uint32_t h = x ^ y ^ z;
-    return Tmask ? (h & Tmask) : (h % T);
-  }
-  return x + y + z;
-}
-__device__ __forceinline__ float corner_weight(const LevelCorners& c, int k) {
-  return ((k & 4) ? c.wx1 : c.wx0) * ((k & 2) ? c.wy1 : c.wy0) * ((k & 1) ? c.wz1 : c.wz0);
-}
-
 // Trilinear hashgrid features of one (position, level) query (hashgrid.h:244-287),
 // accumulated into acc[F].  Each lane may hold a different position and level:
 // the eight corners are unrolled, so the corner choice is resolved at compile
