@@ -121,3 +121,39 @@ def test_exact_restatement_reproduces_the_forward():
     np.testing.assert_allclose(img["out_features"], f["out_features"], atol=1e-4)
     np.testing.assert_allclose(img["visibility"], f["visibility"], atol=1e-4)
     assert np.abs(grads["dL_dmeans3D"]).max() > 0 and np.abs(grads["dL_dfeature_table"]).max() > 0
+
+
+def _lib():
+    import ctypes
+    lib = ctypes.CDLL(os.path.join(PKG, "volume_integration", "libvi_b200.so"))
+    lib.vi_last_error.restype = ctypes.c_char_p
+    return lib
+
+
+def _forward_ex_args(flags, bounds):
+    """Arguments of vi_integrate_primitives_ex for an empty scene (P = 0): the
+    call validates its settings and returns before touching the device."""
+    import ctypes
+    RESIZE = ctypes.CFUNCTYPE(ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t)
+    cb = RESIZE(lambda u, n: 0)
+    vp, f, i, u, u64 = ctypes.c_void_p, ctypes.c_float, ctypes.c_int, ctypes.c_uint, ctypes.c_uint64
+    hb = (ctypes.c_float * 6)(*bounds) if bounds is not None else None
+    R = ctypes.c_int(0)
+    args = [cb, None, cb, None, cb, None, vp(0), vp(0), vp(0), ctypes.byref(R), i(0), vp(0), vp(0), f(0.1), vp(0),
+            vp(0), vp(0), f(1.0), f(1.0), i(0), i(0), f(0.01), f(100.0), vp(0), u64(0), vp(0), vp(0), vp(0), i(64),
+            vp(0), u64(0), vp(0), u64(0), i(1), i(3), i(8), f(0.5), vp(0), u(2), u(4), u(8), u(4), u(3), i(0), vp(0),
+            hb, u(flags)]
+    return args, cb
+
+
+@pytest.mark.parametrize("flags,bounds,msg", [
+    (2, None, b"unknown flags"),
+    (0, (0.0, 0.0, 0.0, 1.0, -1.0, 1.0), b"hash_bounds axis 1"),
+    (0, (0.0, 0.0, 0.0, 1.0, 1.0, float("nan")), b"hash_bounds axis 2"),
+])
+def test_c_abi_rejects_bad_flags_and_bounds(flags, bounds, msg):
+    lib = _lib()
+    args, _keep = _forward_ex_args(flags, bounds)
+    assert lib.vi_integrate_primitives_ex(*args) == 1
+    assert msg in lib.vi_last_error()
+
