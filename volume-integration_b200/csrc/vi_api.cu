@@ -152,7 +152,8 @@ GeomState geom_layout(char* base, size_t P, int V, int O, int D) {
   // Last, so the offsets above do not depend on D.
   g.cls_base = c.take<uint32_t>(P);
   const size_t want = P * (size_t)V;
-  const size_t cap = D > 0 ? std::min(want, phi_cache_max_bytes() / (sizeof(float) * (size_t)D)) : 0;
+  size_t cap = D > 0 ? std::min(want, phi_cache_max_bytes() / (sizeof(float) * (size_t)D)) : 0;
+  cap = std::min(cap, (size_t)kCornerCache - 1);  // the top bit of cls_base marks box-corner primitives
   g.phi_cap = (uint32_t)cap;
   g.phi_cache = c.take<float>(cap * (size_t)D);
   g.bytes = c.size();

@@ -342,7 +342,7 @@ __host__ __device__ inline int bwd_dp(int D) { return pad4(D) + 4; }
 // member masks [32] and the warp's dW partial sums [OMAX][D] (lane j owns
 // columns j, j + 32).
 __host__ __device__ inline int bwd_head_floats(int D, int L, int OMAX) {
-  return OMAX * bwd_dp(D) + OMAX + 3 * pad4(L);
+  return OMAX * bwd_dp(D) + OMAX + 3 * pad4(L) + 8 * bwd_dp(D) + 8 * OMAX;
 }
 __host__ __device__ inline int bwd_warp_floats(int D, int OMAX) {
   return 32 * bwd_dp(D) + 4 * 32 * OMAX + 4 * 32 + 32 + OMAX * D;
@@ -480,6 +480,8 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
   float* resf_s = db_s + OMAX;                            // [L]
   int* res_s = reinterpret_cast<int*>(resf_s + pad4(L));  // [L]
   int* hash_s = res_s + pad4(L);                          // [L]
+  float* cphi_s = reinterpret_cast<float*>(hash_s + pad4(L));  // [8][DP] box-corner features
+  float* cS_s = cphi_s + 8 * DP;  // [8][OMAX] the block's table-gradient coefficients at the box corners
   const int w = threadIdx.x >> 5;
   const uint32_t lane = threadIdx.x & 31;
   float* phi_s = smem + bwd_head_floats(D, L, OMAX) + w * bwd_warp_floats(D, OMAX);  // [32][DP]
@@ -502,12 +504,14 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
     resf_s[i] = (float)sc.res[i];
     hash_s[i] = sc.do_hash[i];
   }
+  for (int i = threadIdx.x; i < 8 * OMAX; i += blockDim.x) cS_s[i] = 0.0f;
   __syncthreads();
 
   const Stencil st = make_stencil(sc.genus);
   const GridPt gpt = grid_point((int)lane < V ? (int)lane : 0, G, sc.gof);
   const uint32_t p0 = (uint32_t)__ldg(sc.primes), p1 = (uint32_t)__ldg(sc.primes + 1),
                  p2 = (uint32_t)__ldg(sc.primes + 2);
+  if (!EXACT) box_corner_features<F>(sc, res_s, resf_s, hash_s, p0, p1, p2, DP, cphi_s);
   const uint32_t lt_mask = (1u << lane) - 1u;
   const uint32_t stride = (uint32_t)D;
   float dbacc = 0.0f;
@@ -727,7 +731,14 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
     }
     __syncwarp();
 
-    if (cached) {
+    const bool corner = cached && (cb & kCornerCache) != 0u;
+    if (corner) {
+      // every grid point clamps to box corner cc: features from the block's
+      // corner vectors, table coefficient summed per block (one class, S_s[0])
+      const int cc = (int)(cb & 7u);
+      for (int i = (int)lane; i < D; i += 32) phi_s[i] = cphi_s[cc * DP + i];
+      if (amask && (int)lane < OMAX) atomicAdd(&cS_s[cc * OMAX + lane], S_s[lane]);
+    } else if (cached) {
       const float* src = g.phi_cache + (size_t)cb * D;
       for (int i = (int)lane; i < pc.U * D; i += 32) phi_s[(i / D) * DP + i % D] = src[i];
     }
@@ -736,7 +747,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
     // level that hit the same table entry share one request.
     const LevelWalk it(pc.U, L);
     float dpos[3] = {0.0f, 0.0f, 0.0f};
-    for (int l0 = 0; l0 < L; l0 += it.per) {
+    for (int l0 = corner ? L : 0; l0 < L; l0 += it.per) {
       if (!it.valid(l0)) continue;
       const int l = it.level(l0), u = it.u;
       const bool doA = (mem_s[u] & (EXACT ? emask : amask)) != 0u;
@@ -854,6 +865,26 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
   __syncwarp();
   if ((int)lane < O && dbacc != 0.0f) atomicAdd(&db_s[lane], dbacc);
   __syncthreads();
+  // Table gradient of the box-corner primitives: one scatter per (corner, level).
+  for (int t = threadIdx.x; t < 8 * L; t += blockDim.x) {
+    const int c = t / L, l = t - (t / L) * L;
+    bool any = false;
+    for (int o = 0; o < OMAX; o++) any |= cS_s[c * OMAX + o] != 0.0f;
+    if (!any) continue;
+    float A[F];
+#pragma unroll
+    for (int f = 0; f < F; f++) {
+      float sum = 0.0f;
+#pragma unroll
+      for (int o = 0; o < OMAX; o++) sum += W_s[o * DP + l * F + f] * cS_s[c * OMAX + o];
+      A[f] = sum;
+    }
+    const LevelCorners lc = level_corners(box_corner_pos(c), res_s[l], resf_s[l], hash_s[l] != 0, p0, p1, p2, sc.T);
+    if (sc.Tmask)
+      scatter_level<F, true>(lc, dtable + (size_t)l * F, stride, sc.T, sc.Tmask, A);
+    else
+      scatter_level<F, false>(lc, dtable + (size_t)l * F, stride, sc.T, sc.Tmask, A);
+  }
   const float* warp0 = smem + bwd_head_floats(D, L, OMAX) + (bwd_warp_floats(D, OMAX) - OMAX * D);
   for (int i = threadIdx.x; i < O * D; i += blockDim.x) {
     float x = 0.0f;

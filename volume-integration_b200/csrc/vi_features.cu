@@ -34,7 +34,7 @@ __host__ __device__ inline int pad4(int x) { return (x + 3) & ~3; }
 // class), class positions [32] float4, and per-lane magnitude, weight and class.
 __host__ __device__ inline int feat_dp(int D) { return pad4(D) + 4; }
 __host__ __device__ inline int feat_head_floats(int D, int L, int OMAX) {
-  return OMAX * feat_dp(D) + OMAX + 3 * pad4(L);
+  return OMAX * feat_dp(D) + OMAX + 3 * pad4(L) + 8 * feat_dp(D) + 8 * OMAX;
 }
 __host__ __device__ inline int feat_warp_floats(int D, int OMAX) { return 32 * feat_dp(D) + 32 * OMAX + 4 * 32 + 3 * 32; }
 
@@ -48,6 +48,8 @@ __global__ void __launch_bounds__(kFeatWarps * 32, 4) features_kernel(Scene sc, 
   float* resf_s = b_s + OMAX;                              // [L] level resolutions as float
   int* res_s = reinterpret_cast<int*>(resf_s + pad4(L));   // [L]
   int* hash_s = res_s + pad4(L);                           // [L]
+  float* cphi_s = reinterpret_cast<float*>(hash_s + pad4(L));  // [8][DP] box-corner features
+  float* cmlp_s = cphi_s + 8 * DP;                             // [8][OMAX] W phi of the box corners
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float* phi_s = smem + feat_head_floats(D, L, OMAX) + w * feat_warp_floats(D, OMAX);  // [32][DP]
   float* mlp_s = phi_s + 32 * DP;                                                    // [32][OMAX]
@@ -66,6 +68,17 @@ __global__ void __launch_bounds__(kFeatWarps * 32, 4) features_kernel(Scene sc, 
   }
   for (int i = threadIdx.x; i < OMAX; i += blockDim.x) b_s[i] = i < O ? sc.bl[i] : 0.0f;
   __syncthreads();
+  {
+    const uint32_t c0 = (uint32_t)__ldg(sc.primes), c1 = (uint32_t)__ldg(sc.primes + 1), c2 = (uint32_t)__ldg(sc.primes + 2);
+    box_corner_features<F>(sc, res_s, resf_s, hash_s, c0, c1, c2, DP, cphi_s);
+    for (int t = threadIdx.x; t < 8 * OMAX; t += blockDim.x) {
+      const int c = t / OMAX, o = t % OMAX;
+      float acc = 0.0f;
+      for (int i = 0; i < D; i++) acc = __fmaf_rn(W_s[o * DP + i], cphi_s[c * DP + i], acc);
+      cmlp_s[t] = acc;
+    }
+    __syncthreads();
+  }
 
   const Stencil st = make_stencil(sc.genus);
   const GridPt gp = grid_point(lane < V ? lane : 0, G, sc.gof);
@@ -117,39 +130,47 @@ __global__ void __launch_bounds__(kFeatWarps * 32, 4) features_kernel(Scene sc, 
         npos_s[pc.cls] = make_float4(n.x, n.y, n.z, 0.0f);
       }
       __syncwarp();
-      const LevelWalk it(pc.U, L);
-      for (int l0 = 0; l0 < L; l0 += it.per) {
-        if (it.valid(l0)) {
-          const int l = it.level(l0);
-          const float4 n4 = npos_s[it.u];
-          const LevelCorners lc = level_corners(make_float3(n4.x, n4.y, n4.z), res_s[l], resf_s[l],
-                                                hash_s[l] != 0, p0, p1, p2, sc.T);
-          float acc[F];
+      const float4 n0 = npos_s[0];
+      if (pc.U == 1 && box_corner(n0)) {
+        // every grid point clamps to one corner of the hashgrid box
+        const int cc = box_corner_index(n0);
+        if (lane < OMAX) mlp_s[lane] = cmlp_s[cc * OMAX + lane];
+        cbase = kCornerCache | (uint32_t)cc;
+      } else {
+        const LevelWalk it(pc.U, L);
+        for (int l0 = 0; l0 < L; l0 += it.per) {
+          if (it.valid(l0)) {
+            const int l = it.level(l0);
+            const float4 n4 = npos_s[it.u];
+            const LevelCorners lc = level_corners(make_float3(n4.x, n4.y, n4.z), res_s[l], resf_s[l],
+                                                  hash_s[l] != 0, p0, p1, p2, sc.T);
+            float acc[F];
 #pragma unroll
-          for (int f = 0; f < F; f++) acc[f] = 0.0f;
-          const float* lvl = sc.table + (size_t)l * F;
-          if (sc.Tmask)
-            gather_level<F, true>(lc, lvl, stride, sc.T, sc.Tmask, acc);
-          else
-            gather_level<F, false>(lc, lvl, stride, sc.T, sc.Tmask, acc);
+            for (int f = 0; f < F; f++) acc[f] = 0.0f;
+            const float* lvl = sc.table + (size_t)l * F;
+            if (sc.Tmask)
+              gather_level<F, true>(lc, lvl, stride, sc.T, sc.Tmask, acc);
+            else
+              gather_level<F, false>(lc, lvl, stride, sc.T, sc.Tmask, acc);
 #pragma unroll
-          for (int f = 0; f < F; f++) phi_s[it.u * DP + l * F + f] = acc[f];
+            for (int f = 0; f < F; f++) phi_s[it.u * DP + l * F + f] = acc[f];
+          }
         }
+        __syncwarp();
+        // Keep the classes' features for the backward: U consecutive slots of
+        // phi_cache from a counter (status[6]), when they fit.
+        if (lane == 0) {
+          const uint32_t b = atomicAdd(g.status + 6, (uint32_t)pc.U);
+          cbase = (uint64_t)b + (uint64_t)pc.U <= (uint64_t)g.phi_cap ? b : kNoCache;
+        }
+        cbase = __shfl_sync(0xffffffffu, cbase, 0);
+        if (cbase != kNoCache) {
+          float* dst = g.phi_cache + (size_t)cbase * D;
+          for (int i = lane; i < pc.U * D; i += 32) dst[i] = phi_s[(i / D) * DP + i % D];
+        }
+        // Linear layer per class: mlp[u][o] = sum_i W[o][i] phi_u[i].
+        class_linear<OMAX>(W_s, phi_s, DP, D, pc.U, mlp_s);
       }
-      __syncwarp();
-      // Keep the classes' features for the backward: U consecutive slots of
-      // phi_cache from a counter (status[6]), when they fit.
-      if (lane == 0) {
-        const uint32_t b = atomicAdd(g.status + 6, (uint32_t)pc.U);
-        cbase = (uint64_t)b + (uint64_t)pc.U <= (uint64_t)g.phi_cap ? b : kNoCache;
-      }
-      cbase = __shfl_sync(0xffffffffu, cbase, 0);
-      if (cbase != kNoCache) {
-        float* dst = g.phi_cache + (size_t)cbase * D;
-        for (int i = lane; i < pc.U * D; i += 32) dst[i] = phi_s[(i / D) * DP + i % D];
-      }
-      // Linear layer per class: mlp[u][o] = sum_i W[o][i] phi_u[i].
-      class_linear<OMAX>(W_s, phi_s, DP, D, pc.U, mlp_s);
       if (need) {
         cls_s[lane] = pc.cls;
         wgt_s[lane] = fmul(conf, mag);

@@ -67,6 +67,9 @@ struct GeomState {
   size_t bytes;
 };
 constexpr uint32_t kNoCache = 0xffffffffu;
+// cls_base of a primitive whose grid points all clamp to box corner c: kCornerCache | c
+// (its features are one of the eight box-corner vectors every block computes).
+constexpr uint32_t kCornerCache = 0x80000000u;
 // Upper bound of phi_cache: every position class of every primitive when that
 // fits, else this many bytes (primitives that find no room gather in the
 // backward).  The environment variable VI_PHI_CACHE_BYTES overrides it (0 turns

@@ -186,6 +186,41 @@ __device__ __forceinline__ void gather_level(const LevelCorners& c, const float*
   }
 }
 
+// The eight corners of the hashgrid box (normalised position in {0, 1}^3;
+// corner c has x = c >> 2, y = (c >> 1) & 1, z = c & 1).  A primitive whose grid
+// points all clamp to one corner reads fixed table entries with weight 1, so a
+// block computes these eight feature vectors once.
+__device__ __forceinline__ bool box_corner(float4 n) {
+  return (n.x == 0.0f || n.x == 1.0f) && (n.y == 0.0f || n.y == 1.0f) && (n.z == 0.0f || n.z == 1.0f);
+}
+__device__ __forceinline__ int box_corner_index(float4 n) {
+  return (n.x == 1.0f ? 4 : 0) | (n.y == 1.0f ? 2 : 0) | (n.z == 1.0f ? 1 : 0);
+}
+__device__ __forceinline__ float3 box_corner_pos(int c) {
+  return make_float3((float)((c >> 2) & 1), (float)((c >> 1) & 1), (float)(c & 1));
+}
+// cphi[c * DP + l * F + f] for the 8 corners; the whole block, ends with a barrier.
+template <int F>
+__device__ void box_corner_features(const Scene& sc, const int* res_s, const float* resf_s, const int* hash_s,
+                                    uint32_t p0, uint32_t p1, uint32_t p2, int DP, float* cphi) {
+  const int L = sc.L;
+  for (int t = threadIdx.x; t < 8 * L; t += blockDim.x) {
+    const int c = t / L, l = t - (t / L) * L;
+    const LevelCorners lc = level_corners(box_corner_pos(c), res_s[l], resf_s[l], hash_s[l] != 0, p0, p1, p2, sc.T);
+    float acc[F];
+#pragma unroll
+    for (int f = 0; f < F; f++) acc[f] = 0.0f;
+    const float* lvl = sc.table + (size_t)l * F;
+    if (sc.Tmask)
+      gather_level<F, true>(lc, lvl, (uint32_t)(L * F), sc.T, sc.Tmask, acc);
+    else
+      gather_level<F, false>(lc, lvl, (uint32_t)(L * F), sc.T, sc.Tmask, acc);
+#pragma unroll
+    for (int f = 0; f < F; f++) cphi[c * DP + l * F + f] = acc[f];
+  }
+  __syncthreads();
+}
+
 // Lanes of a warp grouped by bit-identical normalised hashgrid position: every
 // member of a class reads the same table entries with the same weights, so the
 // class's features are gathered once.  Points clamped to a face of the fixed
