@@ -103,6 +103,14 @@ cudaEvent_t prof_event() {
 
 void note_launches(int n) { g_launch_count.fetch_add((unsigned long long)n, std::memory_order_relaxed); }
 
+int resident_blocks(const void* kernel, int threads, size_t smem) {
+  int dev = 0, sms = 0, per = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kernel, threads, smem);
+  return (sms > 0 ? sms : 1) * (per > 0 ? per : 1);
+}
+
 void stage_begin(Stage st, cudaStream_t s) {
   if (!g_prof_on) return;
   std::lock_guard<std::mutex> lk(g_prof_mu);

@@ -903,8 +903,10 @@ void launch_prim_t(const Scene& sc, GeomState& g, float* dmeans, float* dconf, f
   auto k = sc.exact ? backward_prim_kernel<F, OMAX, true> : backward_prim_kernel<F, OMAX, false>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   cudaMemsetAsync(g.status + 5, 0, sizeof(uint32_t), s);
+  // A resident grid: warps draw primitives from the counter until it runs out.
   int blocks = (sc.P + kBwdWarps - 1) / kBwdWarps;
-  blocks = blocks < 148 * 10 ? blocks : 148 * 10;
+  const int resident = resident_blocks(reinterpret_cast<const void*>(k), kBwdWarps * 32, smem);
+  blocks = blocks < resident ? blocks : resident;
   if (blocks < 1) blocks = 1;
   k<<<blocks, kBwdWarps * 32, smem, s>>>(sc, g, dmeans, dconf, dtable, dW, db);
   note_launches(1);

@@ -38,8 +38,9 @@ __host__ __device__ inline int feat_head_floats(int D, int L, int OMAX) {
 }
 __host__ __device__ inline int feat_warp_floats(int D, int OMAX) { return 32 * feat_dp(D) + 32 * OMAX + 4 * 32 + 3 * 32; }
 
-template <int F, int OMAX>
-__global__ void __launch_bounds__(kFeatWarps * 32, 4) features_kernel(Scene sc, GeomState g) {
+// POW2: the table size T is a power of two (hash modulo by mask).
+template <int F, int OMAX, bool POW2>
+__global__ void __launch_bounds__(kFeatWarps * 32, 3) features_kernel(Scene sc, GeomState g) {
   extern __shared__ float4 smem4[];
   float* smem = reinterpret_cast<float*>(smem4);
   const int L = sc.L, D = L * F, DP = feat_dp(D), O = sc.O, V = sc.V, G = sc.G;
@@ -137,33 +138,47 @@ __global__ void __launch_bounds__(kFeatWarps * 32, 4) features_kernel(Scene sc, 
         if (lane < OMAX) mlp_s[lane] = cmlp_s[cc * OMAX + lane];
         cbase = kCornerCache | (uint32_t)cc;
       } else {
+        // Two steps of the level walk at a time, so that each lane has the
+        // loads of two (class, level) items in flight.
         const LevelWalk it(pc.U, L);
-        for (int l0 = 0; l0 < L; l0 += it.per) {
-          if (it.valid(l0)) {
-            const int l = it.level(l0);
-            const float4 n4 = npos_s[it.u];
-            const LevelCorners lc = level_corners(make_float3(n4.x, n4.y, n4.z), res_s[l], resf_s[l],
-                                                  hash_s[l] != 0, p0, p1, p2, sc.T);
-            float acc[F];
+        for (int l0 = 0; l0 < L; l0 += 2 * it.per) {
+          const bool v0 = it.valid(l0), v1 = it.valid(l0 + it.per);
+          const float4 n4 = npos_s[it.u];
+          const float3 nn = make_float3(n4.x, n4.y, n4.z);
+          const int la = it.level(l0), lb = it.level(l0 + it.per);
+          float acc0[F], acc1[F];
 #pragma unroll
-            for (int f = 0; f < F; f++) acc[f] = 0.0f;
-            const float* lvl = sc.table + (size_t)l * F;
-            if (sc.Tmask)
-              gather_level<F, true>(lc, lvl, stride, sc.T, sc.Tmask, acc);
-            else
-              gather_level<F, false>(lc, lvl, stride, sc.T, sc.Tmask, acc);
+          for (int f = 0; f < F; f++) acc0[f] = acc1[f] = 0.0f;
+          if (v0) {
+            const LevelCorners lc = level_corners(nn, res_s[la], resf_s[la], hash_s[la] != 0, p0, p1, p2, sc.T);
+            gather_level<F, POW2>(lc, sc.table + (size_t)la * F, stride, sc.T, sc.Tmask, acc0);
+          }
+          if (v1) {
+            const LevelCorners lc = level_corners(nn, res_s[lb], resf_s[lb], hash_s[lb] != 0, p0, p1, p2, sc.T);
+            gather_level<F, POW2>(lc, sc.table + (size_t)lb * F, stride, sc.T, sc.Tmask, acc1);
+          }
+          if (v0) {
 #pragma unroll
-            for (int f = 0; f < F; f++) phi_s[it.u * DP + l * F + f] = acc[f];
+            for (int f = 0; f < F; f++) phi_s[it.u * DP + la * F + f] = acc0[f];
+          }
+          if (v1) {
+#pragma unroll
+            for (int f = 0; f < F; f++) phi_s[it.u * DP + lb * F + f] = acc1[f];
           }
         }
         __syncwarp();
-        // Keep the classes' features for the backward: U consecutive slots of
-        // phi_cache from a counter (status[6]), when they fit.
-        if (lane == 0) {
-          const uint32_t b = atomicAdd(g.status + 6, (uint32_t)pc.U);
-          cbase = (uint64_t)b + (uint64_t)pc.U <= (uint64_t)g.phi_cap ? b : kNoCache;
+        // Keep the classes' features for the backward in phi_cache: slots
+        // [q*V, q*V + U) when the cache holds V slots per primitive, else U
+        // consecutive slots from a counter (status[6]) while they fit.
+        if ((uint64_t)g.phi_cap >= (uint64_t)sc.P * (uint64_t)V) {
+          cbase = (uint32_t)q * (uint32_t)V;
+        } else {
+          if (lane == 0) {
+            const uint32_t b = atomicAdd(g.status + 6, (uint32_t)pc.U);
+            cbase = (uint64_t)b + (uint64_t)pc.U <= (uint64_t)g.phi_cap ? b : kNoCache;
+          }
+          cbase = __shfl_sync(0xffffffffu, cbase, 0);
         }
-        cbase = __shfl_sync(0xffffffffu, cbase, 0);
         if (cbase != kNoCache) {
           float* dst = g.phi_cache + (size_t)cbase * D;
           for (int i = lane; i < pc.U * D; i += 32) dst[i] = phi_s[(i / D) * DP + i % D];
@@ -244,17 +259,28 @@ __global__ void __launch_bounds__(kFeatWarps * 32, 4) features_kernel(Scene sc, 
   }
 }
 
-template <int F, int OMAX>
-void launch_features_t(const Scene& sc, GeomState& g, cudaStream_t s) {
+template <int F, int OMAX, bool POW2>
+void launch_features_p(const Scene& sc, GeomState& g, cudaStream_t s) {
   const int D = sc.L * F;
   size_t smem = sizeof(float) * (feat_head_floats(D, sc.L, OMAX) + kFeatWarps * feat_warp_floats(D, OMAX));
-  auto k = features_kernel<F, OMAX>;
+  auto k = features_kernel<F, OMAX, POW2>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  // A resident grid: every warp loops over primitives with the same stride,
+  // so a second partial wave would only lengthen the stage.
   int blocks = (sc.P + kFeatWarps - 1) / kFeatWarps;
-  blocks = blocks < 148 * 8 ? blocks : 148 * 8;
+  const int resident = resident_blocks(reinterpret_cast<const void*>(k), kFeatWarps * 32, smem);
+  blocks = blocks < resident ? blocks : resident;
   if (blocks < 1) blocks = 1;
   k<<<blocks, kFeatWarps * 32, smem, s>>>(sc, g);
   note_launches(1);
+}
+
+template <int F, int OMAX>
+void launch_features_t(const Scene& sc, GeomState& g, cudaStream_t s) {
+  if (sc.Tmask)
+    launch_features_p<F, OMAX, true>(sc, g, s);
+  else
+    launch_features_p<F, OMAX, false>(sc, g, s);
 }
 
 }  // namespace

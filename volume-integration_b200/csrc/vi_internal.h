@@ -15,6 +15,11 @@ inline size_t align_up(size_t x, size_t a = 256) { return (x + a - 1) / a * a; }
 // Number of kernels this library has launched (all threads), for launch accounting.
 void note_launches(int n);
 
+// Blocks of `threads` threads and `smem` dynamic shared bytes that the current
+// device holds resident at once (SM count x blocks per SM), for persistent
+// grids that loop over their work.
+int resident_blocks(const void* kernel, int threads, size_t smem);
+
 // Optional per-stage CUDA-event timing on the launching stream.
 enum Stage { kStPreprocess, kStDepthSort, kStOffsets, kStFeatures, kStBinning, kStRender, kStBwdPixel, kStBwdPrim,
              kStCount };
