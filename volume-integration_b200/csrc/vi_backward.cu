@@ -523,26 +523,48 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
 
   // Primitives are handed out in batches of kGrab per warp from a counter
   // (status[5]): warps that draw cheap primitives take more, so no warp idles at
-  // the final reduction while the counter sees one atomic per batch.
+  // the final reduction while the counter sees one atomic per batch.  The
+  // batch's record counts (one load) pick the primitives with records, and the
+  // inputs of the next one are loaded while the current one is processed.
   constexpr int kGrab = 8;
-  for (int q0 = 0, qi = kGrab;;) {
-    if (qi == kGrab) {
-      if (lane == 0) q0 = (int)atomicAdd(g.status + 5, (unsigned)kGrab);
-      q0 = __shfl_sync(0xffffffffu, q0, 0);
-      qi = 0;
-    }
-    const int q = q0 + qi++;
-    if (q >= sc.P) break;
+  const bool act = (int)lane < V;
+  uint32_t rp_next = 0u;
+  float conf_next = 0.0f;
+  float3 c_next = make_float3(0.0f, 0.0f, 0.0f);
+  int q_next = -1;
+  for (;;) {
+    int q0 = 0;
+    if (lane == 0) q0 = (int)atomicAdd(g.status + 5, (unsigned)kGrab);
+    q0 = __shfl_sync(0xffffffffu, q0, 0);
+    if (q0 >= sc.P) break;
+    const uint32_t cnt = (int)lane < kGrab && q0 + (int)lane < sc.P ? g.rec_cnt[q0 + lane] : 0u;
+    uint32_t batch = __ballot_sync(0xffffffffu, (cnt & ~kBwdDiffers) != 0u);
+    while (batch) {
+    const int q = q0 + __ffs(batch) - 1;
+    batch &= batch - 1;
     const size_t s0 = (size_t)q * V;
-    // rec_pix is zero except in slots of contributing records (the record count
-    // need not be read first).
-    const uint32_t rp = (int)lane < V ? g.rec_pix[s0 + lane] : 0u;
+    uint32_t rp;  // pixel + 1 of each grid point's contributing record, else 0
+    float conf;
+    float3 c;
+    if (q_next == q) {
+      rp = rp_next;
+      conf = conf_next;
+      c = c_next;
+    } else {
+      rp = act ? g.rec_pix[s0 + lane] : 0u;
+      conf = act ? sc.conf[s0 + lane] : 0.0f;
+      c = make_float3(sc.means[3 * q], sc.means[3 * q + 1], sc.means[3 * q + 2]);
+    }
+    if (batch) {
+      q_next = q0 + __ffs(batch) - 1;
+      const size_t s1 = (size_t)q_next * V;
+      rp_next = act ? g.rec_pix[s1 + lane] : 0u;
+      conf_next = act ? sc.conf[s1 + lane] : 0.0f;
+      c_next = make_float3(sc.means[3 * q_next], sc.means[3 * q_next + 1], sc.means[3 * q_next + 2]);
+    }
     const uint32_t cm = __ballot_sync(0xffffffffu, rp != 0u);
     if (cm == 0) continue;
 
-    const bool act = (int)lane < V;
-    const float conf = act ? sc.conf[s0 + lane] : 0.0f;
-    const float3 c = make_float3(sc.means[3 * q], sc.means[3 * q + 1], sc.means[3 * q + 2]);
     const float3 pos = grid_pos_rel(c, gpt.rel, sc.step);
     // the reference's backward recomputes screen positions with 1/w
     // (backward.cu:325); the exact mode follows the forward's 1/(w + 1e-7)
@@ -855,6 +877,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
       }
     }
     __syncwarp();
+    }
   }
 
   // CTA reduction of dW and db, then one global atomic per element.
