@@ -88,16 +88,27 @@ __global__ void __launch_bounds__(kFeatWarps * 32, 3) features_kernel(Scene sc, 
                  p2 = (uint32_t)__ldg(sc.primes + 2);
   const uint32_t stride = (uint32_t)D;
   const int OP = OMAX;
-  const int nwarps = gridDim.x * kFeatWarps;
-  for (int q = blockIdx.x * kFeatWarps + w; q < sc.P; q += nwarps) {
-    const int r = g.radii[q];
-    if (r <= 0) {
-      if (lane == 0) {
-        g.rec_cnt[q] = 0;
-        g.cls_base[q] = kNoCache;
-      }
-      continue;
+  // Warps claim chunks of 32 consecutive primitives from a counter (status[4]):
+  // the cost of a primitive varies widely, so a fixed share per warp would
+  // leave most warps idle at the end.  One radii load per chunk picks its
+  // visible primitives.
+  for (;;) {
+    int ch = 0;
+    if (lane == 0) ch = (int)atomicAdd(g.status + 4, 1u);
+    const int qb = __shfl_sync(0xffffffffu, ch, 0) * 32;
+    if (qb >= sc.P) break;
+    const int ql = qb + lane;
+    const int rl = ql < sc.P ? g.radii[ql] : 0;
+    if (ql < sc.P && rl <= 0) {
+      g.rec_cnt[ql] = 0;
+      g.cls_base[ql] = kNoCache;
     }
+    uint32_t vis = __ballot_sync(0xffffffffu, rl > 0);
+    while (vis) {
+    const int qi = __ffs(vis) - 1;
+    vis &= vis - 1;
+    const int q = qb + qi;
+    const int r = __shfl_sync(0xffffffffu, rl, qi);
     const float3 c = make_float3(sc.means[3 * q], sc.means[3 * q + 1], sc.means[3 * q + 2]);
     const float2 m2 = make_float2(g.means2D[2 * q], g.means2D[2 * q + 1]);
     // getRect with the same float arithmetic as preprocess (auxiliary.h:55-65).
@@ -256,6 +267,7 @@ __global__ void __launch_bounds__(kFeatWarps * 32, 3) features_kernel(Scene sc, 
       g.cls_base[q] = cbase;
     }
     __syncwarp();
+    }
   }
 }
 
@@ -265,9 +277,8 @@ void launch_features_p(const Scene& sc, GeomState& g, cudaStream_t s) {
   size_t smem = sizeof(float) * (feat_head_floats(D, sc.L, OMAX) + kFeatWarps * feat_warp_floats(D, OMAX));
   auto k = features_kernel<F, OMAX, POW2>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  // A resident grid: every warp loops over primitives with the same stride,
-  // so a second partial wave would only lengthen the stage.
-  int blocks = (sc.P + kFeatWarps - 1) / kFeatWarps;
+  // A resident grid: warps claim chunks until the counter runs out.
+  int blocks = ((sc.P + 31) / 32 + kFeatWarps - 1) / kFeatWarps;
   const int resident = resident_blocks(reinterpret_cast<const void*>(k), kFeatWarps * 32, smem);
   blocks = blocks < resident ? blocks : resident;
   if (blocks < 1) blocks = 1;

@@ -49,7 +49,7 @@ bool onesweep_sort_u64(uint64_t* keys, uint32_t* vals, uint64_t* alt_keys, uint3
 // Geometry state: everything sized by the primitive count P.
 // ---------------------------------------------------------------------------
 struct GeomState {
-  uint32_t* status;          // [0] status bits, [2..3] num_rendered as u64, [4] [5] work counters, [6] phi_cache slots used
+  uint32_t* status;          // [0] status bits, [2..3] num_rendered as u64, [4] feature-stage chunk counter, [5] backward work counter, [6] phi_cache slots used
   float* depths;             // [P] view-space z of the centre
   int* radii;                // [P]
   float* means2D;            // [2P]
