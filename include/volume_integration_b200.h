@@ -192,6 +192,67 @@ typedef struct vi_state_layout {
 int vi_get_state_layout(int P, int64_t num_rendered, int image_height, int image_width, int max_primitives_per_ray,
                         int grid_size, unsigned output_feature_dim, vi_state_layout* out);
 
+/*
+ * ---- Gaussian-attribute front end (extension) ----
+ * No counterpart in the reference: its primitives are cubes of one fixed world
+ * size, projected by centre and bounding radius only
+ * (cuda_integrator/forward.cu:82-87, :100-102; the spherical-harmonics
+ * constants of cuda_integrator/auxiliary.h:30-48 are unused).  These entry
+ * points are the standard per-Gaussian front end of splatting: projection, 3D
+ * and 2D covariance (EWA, with the 0.3 pixel low-pass), conic, radius and tiles
+ * touched, and colour from real spherical harmonics of degree 0..3.
+ *
+ * Layouts (row-major, float32 unless noted): means3D, scales [P][3];
+ * rotations [P][4] quaternions (r, x, y, z), 16-byte aligned; opacities [P];
+ * shs [P][sh_coeffs][3] with (sh_degree+1)^2 <= sh_coeffs <= 16; viewmatrix and
+ * projmatrix as the renderer's (device pointers); cam_pos_host is a HOST
+ * pointer to 3 floats.  Outputs: radii [P] int32 (0 = culled), means2D [P][2],
+ * depths [P] (view-space z), cov3D [P][6] (xx, xy, xz, yy, yz, zz),
+ * conic_opacity [P][4] (inverse 2D covariance a, b, c and the opacity; 16-byte
+ * aligned), rgb [P][3], clamped [P][3] uint8 (colour clamped at 0), and
+ * tiles_touched [P] uint32.  Culled Gaussians (t.z <= near_plane, singular 2D
+ * covariance or an empty tile rectangle) have every output zero.
+ */
+int vi_preprocess_gaussians(int P, int sh_degree, int sh_coeffs, const float* means3D, const float* scales,
+                            const float* rotations, const float* opacities, const float* shs, float scale_modifier,
+                            const float* viewmatrix, const float* projmatrix, const float* cam_pos_host,
+                            int image_width, int image_height, float tan_fovx, float tan_fovy, float near_plane,
+                            int* radii, float* means2D, float* depths, float* cov3D, float* conic_opacity, float* rgb,
+                            uint8_t* clamped, uint32_t* tiles_touched, void* stream);
+
+/*
+ * Exact derivative of vi_preprocess_gaussians.  Incoming gradients: means2D
+ * [P][2], depths [P] (may be NULL), cov3D [P][6], conic_opacity [P][4] (the
+ * fourth component, the opacity's, is not used: it passes through to
+ * opacities unchanged), rgb [P][3].  Writes dL/dmeans3D [P][3], dL/dscales
+ * [P][3], dL/drotations [P][4] (16-byte aligned) and dL/dshs [P][sh_coeffs][3];
+ * culled Gaussians (radii == 0) get zeros.
+ */
+int vi_preprocess_gaussians_backward(int P, int sh_degree, int sh_coeffs, const float* means3D, const float* scales,
+                                     const float* rotations, const float* shs, float scale_modifier,
+                                     const float* viewmatrix, const float* projmatrix, const float* cam_pos_host,
+                                     int image_width, int image_height, float tan_fovx, float tan_fovy,
+                                     float near_plane, const int* radii, const uint8_t* clamped,
+                                     const float* dL_dmeans2D, const float* dL_ddepths, const float* dL_dcov3D,
+                                     const float* dL_dconic_opacity, const float* dL_drgb, float* dL_dmeans3D,
+                                     float* dL_dscales, float* dL_drotations, float* dL_dshs, void* stream);
+
+/*
+ * Tile binning of projected Gaussians: the point list sorted by (tile, depth,
+ * index) and per-tile [start, end) ranges, the same result as the reference
+ * renderer's duplicateWithKeys + 64-bit radix sort + identifyTileRanges
+ * (cuda_integrator/integrator_impl.cu:106-178) applied to these Gaussians.
+ * num_rendered must equal the sum of tiles_touched (checked after the scan,
+ * which blocks the host; a mismatch is an error).  scratch is 256-byte
+ * aligned device memory of vi_bin_gaussians_scratch_bytes(); point_list and
+ * tile_ids (optional) hold num_rendered entries, ranges 2 * tiles.
+ */
+uint64_t vi_bin_gaussians_scratch_bytes(int P, uint64_t num_rendered, int image_width, int image_height);
+int vi_bin_gaussians(int P, int image_width, int image_height, const int* radii, const float* means2D,
+                     const float* depths, const uint32_t* tiles_touched, uint64_t num_rendered, void* scratch,
+                     uint64_t scratch_bytes, uint32_t* point_list, uint32_t* tile_ids, uint32_t* ranges,
+                     void* stream);
+
 /* Reads the status word a forward latched in its geometry buffer (blocks). */
 int vi_read_device_status(const char* geom_buffer, uint32_t* status, void* stream);
 

@@ -247,6 +247,113 @@ std::tuple<Tensor, Tensor> sort_pairs(const Tensor& keys, const Tensor& vals, in
 
 }  // namespace
 
+// ---- Gaussian-attribute front end (extension; no counterpart in the reference) ----
+
+Tensor aligned16(const Tensor& t) {
+  Tensor c = cuda_f32(t, "tensor");
+  if (reinterpret_cast<uintptr_t>(c.data_ptr()) % 16 != 0) c = c.clone();
+  return c;
+}
+
+std::vector<float> host3(const Tensor& t) {
+  Tensor h = t.detach().to(torch::kCPU, torch::kFloat32).contiguous().view({-1});
+  TORCH_CHECK(h.numel() == 3, "campos must hold 3 values");
+  return {h[0].item<float>(), h[1].item<float>(), h[2].item<float>()};
+}
+
+// (radii, means2D, depths, cov3D, conic_opacity, rgb, clamped, tiles_touched)
+std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor> preprocess_gaussians(
+    const Tensor& means3D, const Tensor& scales, const Tensor& rotations, const Tensor& opacities, const Tensor& shs,
+    int64_t sh_degree, double scale_modifier, const Tensor& viewmatrix, const Tensor& projmatrix, const Tensor& campos,
+    int64_t image_width, int64_t image_height, double tan_fovx, double tan_fovy, double near_plane) {
+  const at::cuda::OptionalCUDAGuard guard(means3D.device());
+  Tensor m = cuda_f32(means3D, "means3D"), sc = cuda_f32(scales, "scales"), q = aligned16(rotations);
+  Tensor op = cuda_f32(opacities, "opacities"), sh = cuda_f32(shs, "shs");
+  Tensor vm = cuda_f32(viewmatrix, "viewmatrix"), pm = cuda_f32(projmatrix, "projmatrix");
+  const int64_t P = m.size(0);
+  TORCH_CHECK(m.dim() == 2 && m.size(1) == 3 && sc.sizes() == m.sizes(), "means3D and scales must be [P, 3]");
+  TORCH_CHECK(q.dim() == 2 && q.size(0) == P && q.size(1) == 4, "rotations must be [P, 4]");
+  TORCH_CHECK(op.numel() == P, "opacities must hold P values");
+  TORCH_CHECK(sh.dim() == 3 && sh.size(0) == P && sh.size(2) == 3, "shs must be [P, M, 3]");
+  const std::vector<float> cp = host3(campos);
+  auto f32 = m.options();
+  Tensor radii = torch::empty({P}, f32.dtype(torch::kInt32));
+  Tensor means2D = torch::empty({P, 2}, f32), depths = torch::empty({P}, f32), cov3D = torch::empty({P, 6}, f32);
+  Tensor conic = torch::empty({P, 4}, f32), rgb = torch::empty({P, 3}, f32);
+  Tensor clamped = torch::empty({P, 3}, f32.dtype(torch::kUInt8));
+  Tensor tiles = torch::empty({P}, f32.dtype(torch::kInt32));
+  ok(vi_preprocess_gaussians((int)P, (int)sh_degree, (int)sh.size(1), m.data_ptr<float>(), sc.data_ptr<float>(),
+                             q.data_ptr<float>(), op.data_ptr<float>(), sh.data_ptr<float>(), (float)scale_modifier,
+                             vm.data_ptr<float>(), pm.data_ptr<float>(), cp.data(), (int)image_width,
+                             (int)image_height, (float)tan_fovx, (float)tan_fovy, (float)near_plane,
+                             radii.data_ptr<int>(), means2D.data_ptr<float>(), depths.data_ptr<float>(),
+                             cov3D.data_ptr<float>(), conic.data_ptr<float>(), rgb.data_ptr<float>(),
+                             reinterpret_cast<uint8_t*>(clamped.data_ptr()),
+                             reinterpret_cast<uint32_t*>(tiles.data_ptr()), at::cuda::getCurrentCUDAStream().stream()));
+  return {radii, means2D, depths, cov3D, conic, rgb, clamped, tiles};
+}
+
+// (dL/dmeans3D, dL/dscales, dL/drotations, dL/dshs)
+std::tuple<Tensor, Tensor, Tensor, Tensor> preprocess_gaussians_backward(
+    const Tensor& means3D, const Tensor& scales, const Tensor& rotations, const Tensor& shs, int64_t sh_degree,
+    double scale_modifier, const Tensor& viewmatrix, const Tensor& projmatrix, const Tensor& campos,
+    int64_t image_width, int64_t image_height, double tan_fovx, double tan_fovy, double near_plane,
+    const Tensor& radii, const Tensor& clamped, const Tensor& dL_dmeans2D, const Tensor& dL_ddepths,
+    const Tensor& dL_dcov3D, const Tensor& dL_dconic_opacity, const Tensor& dL_drgb) {
+  const at::cuda::OptionalCUDAGuard guard(means3D.device());
+  Tensor m = cuda_f32(means3D, "means3D"), sc = cuda_f32(scales, "scales"), q = aligned16(rotations);
+  Tensor sh = cuda_f32(shs, "shs");
+  Tensor vm = cuda_f32(viewmatrix, "viewmatrix"), pm = cuda_f32(projmatrix, "projmatrix");
+  Tensor rd = cuda_i32(radii, "radii");
+  TORCH_CHECK(clamped.is_cuda() && clamped.scalar_type() == torch::kUInt8, "clamped must be a CUDA uint8 tensor");
+  Tensor cl = clamped.contiguous();
+  const int64_t P = m.size(0);
+  Tensor g2 = cuda_f32(dL_dmeans2D, "dL_dmeans2D"), gd = cuda_f32(dL_ddepths, "dL_ddepths");
+  Tensor gcov = cuda_f32(dL_dcov3D, "dL_dcov3D"), gco = cuda_f32(dL_dconic_opacity, "dL_dconic_opacity");
+  Tensor grgb = cuda_f32(dL_drgb, "dL_drgb");
+  TORCH_CHECK(g2.numel() == 2 * P && gd.numel() == P && gcov.numel() == 6 * P && gco.numel() == 4 * P &&
+                  grgb.numel() == 3 * P && rd.numel() == P && cl.numel() == 3 * P,
+              "gradient shapes do not match P");
+  const std::vector<float> cp = host3(campos);
+  Tensor dm = torch::empty({P, 3}, m.options()), ds = torch::empty({P, 3}, m.options());
+  Tensor dq = torch::empty({P, 4}, m.options()), dsh = torch::empty_like(sh);
+  ok(vi_preprocess_gaussians_backward(
+      (int)P, (int)sh_degree, (int)sh.size(1), m.data_ptr<float>(), sc.data_ptr<float>(), q.data_ptr<float>(),
+      sh.data_ptr<float>(), (float)scale_modifier, vm.data_ptr<float>(), pm.data_ptr<float>(), cp.data(),
+      (int)image_width, (int)image_height, (float)tan_fovx, (float)tan_fovy, (float)near_plane, rd.data_ptr<int>(),
+      reinterpret_cast<const uint8_t*>(cl.data_ptr()), g2.data_ptr<float>(), gd.data_ptr<float>(),
+      gcov.data_ptr<float>(), gco.data_ptr<float>(), grgb.data_ptr<float>(), dm.data_ptr<float>(),
+      ds.data_ptr<float>(), dq.data_ptr<float>(), dsh.data_ptr<float>(), at::cuda::getCurrentCUDAStream().stream()));
+  return {dm, ds, dq, dsh};
+}
+
+// (point_list [R] int32, tile ids [R] int32, ranges [tiles, 2] int32)
+std::tuple<Tensor, Tensor, Tensor> bin_gaussians(const Tensor& radii, const Tensor& means2D, const Tensor& depths,
+                                                 const Tensor& tiles_touched, int64_t image_width,
+                                                 int64_t image_height) {
+  const at::cuda::OptionalCUDAGuard guard(radii.device());
+  Tensor rd = cuda_i32(radii, "radii"), m2 = cuda_f32(means2D, "means2D"), dp = cuda_f32(depths, "depths");
+  Tensor tt = cuda_i32(tiles_touched, "tiles_touched");
+  const int64_t P = rd.numel();
+  TORCH_CHECK(m2.numel() == 2 * P && dp.numel() == P && tt.numel() == P, "binning inputs must describe P Gaussians");
+  const int64_t R = P ? tt.sum(torch::kInt64).item<int64_t>() : 0;  // buffer sizing; the scan re-checks it
+  const int64_t tiles = ((image_width + 15) / 16) * ((image_height + 15) / 16);
+  auto i32 = rd.options();
+  Tensor point_list = torch::empty({R}, i32), tile_ids = torch::empty({R}, i32);
+  Tensor ranges = torch::empty({tiles, 2}, i32);
+  const uint64_t nbytes = vi_bin_gaussians_scratch_bytes((int)P, (uint64_t)R, (int)image_width, (int)image_height);
+  TORCH_CHECK(nbytes > 0, "volume_integration: bad binning sizes");
+  Tensor scratch = torch::empty({(int64_t)nbytes + 256}, rd.options().dtype(torch::kUInt8));
+  char* base = reinterpret_cast<char*>(scratch.data_ptr());
+  char* al = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(base) + 255) & ~uintptr_t(255));
+  ok(vi_bin_gaussians((int)P, (int)image_width, (int)image_height, rd.data_ptr<int>(), m2.data_ptr<float>(),
+                      dp.data_ptr<float>(), reinterpret_cast<const uint32_t*>(tt.data_ptr()), (uint64_t)R, al, nbytes,
+                      R ? reinterpret_cast<uint32_t*>(point_list.data_ptr()) : nullptr,
+                      R ? reinterpret_cast<uint32_t*>(tile_ids.data_ptr()) : nullptr,
+                      reinterpret_cast<uint32_t*>(ranges.data_ptr()), at::cuda::getCurrentCUDAStream().stream()));
+  return {point_list, tile_ids, ranges};
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("integrate_primitives", &integrate_primitives, "Integrate Primitives CUDA forward");
   m.def("integrate_primitives_backward", &integrate_primitives_backward, "Integrate Primitives CUDA backward");
@@ -257,6 +364,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "integrate_primitives_backward plus the hashgrid box, flags and dL/dvisibility (empty = none)");
   m.attr("FLAG_EXACT_GRADIENTS") = (int64_t)VI_FLAG_EXACT_GRADIENTS;
   m.def("mark_visible", &mark_visible, "Mark Visible Primitives CUDA");
+  m.def("preprocess_gaussians", &preprocess_gaussians, "Gaussian-attribute preprocess (extension)");
+  m.def("preprocess_gaussians_backward", &preprocess_gaussians_backward,
+        "Exact derivative of the Gaussian-attribute preprocess (extension)");
+  m.def("bin_gaussians", &bin_gaussians, "Tile binning of projected Gaussians (extension)");
   m.def("state_views", &state_views, "Integer state of a forward call in the reference's formats");
   m.def("sort_pairs", &sort_pairs, "Stable radix sort of (uint64 key, uint32 value) pairs");
   m.def("sort_end_bit", [](int64_t tiles) { return vi_sort_end_bit((uint32_t)tiles); });

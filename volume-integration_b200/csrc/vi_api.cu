@@ -51,16 +51,6 @@ struct Carver {
 };
 
 int props_stride(int O) { return O > 8 ? 16 : 8; }
-int tile_bits(size_t tiles) {
-  // getHigherMsb (integrator_impl.cu:47-62)
-  uint32_t n = (uint32_t)tiles, msb = sizeof(n) * 4, step = msb;
-  while (step > 1) {
-    step /= 2;
-    if (n >> msb) msb += step; else msb -= step;
-  }
-  if (n >> msb) msb++;
-  return (int)msb;
-}
 
 thread_local uint64_t* g_pinned = nullptr;
 thread_local cudaEvent_t g_events[64] = {};
@@ -268,6 +258,18 @@ int check(cudaStream_t s, int debug, const char* where, const uint32_t* status) 
 
 // Records a message for vi_last_error() and returns code (for other translation units).
 int set_error(int code, const char* msg) { return fail(code, "%s", msg); }
+
+int tile_bits(size_t tiles) {
+  // getHigherMsb (integrator_impl.cu:47-62)
+  uint32_t n = (uint32_t)tiles, msb = sizeof(n) * 4, step = msb;
+  while (step > 1) {
+    step /= 2;
+    if (n >> msb) msb += step; else msb -= step;
+  }
+  if (n >> msb) msb++;
+  return (int)msb;
+}
+
 
 }  // namespace vi
 

@@ -22,22 +22,6 @@
 namespace vi {
 namespace {
 
-// getRect (auxiliary.h:55-65), with the float conversions of the reference.  The
-// division by the tile size 16 is written as a multiplication by 0.0625: both
-// round the same exact value x * 2^-4, so the result is identical.
-__device__ __forceinline__ void get_rect(float2 p, int r, unsigned gx, unsigned gy, uint2& mn, uint2& mx) {
-  float rf = (float)r;
-  int a;
-  a = max(0, (int)(fmul(fsub(p.x, rf), 0.0625f)));
-  mn.x = min(gx, (unsigned)a);
-  a = max(0, (int)(fmul(fsub(p.y, rf), 0.0625f)));
-  mn.y = min(gy, (unsigned)a);
-  a = max(0, (int)(fmul(fsub(fadd(fadd(p.x, rf), (float)VI_TILE), 1.0f), 0.0625f)));
-  mx.x = min(gx, (unsigned)a);
-  a = max(0, (int)(fmul(fsub(fadd(fadd(p.y, rf), (float)VI_TILE), 1.0f), 0.0625f)));
-  mx.y = min(gy, (unsigned)a);
-}
-
 __global__ void __launch_bounds__(256) preprocess_kernel(Scene sc, GeomState g) {
   int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= sc.P) return;

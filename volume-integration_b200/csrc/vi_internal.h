@@ -15,6 +15,12 @@ inline size_t align_up(size_t x, size_t a = 256) { return (x + a - 1) / a * a; }
 // Number of kernels this library has launched (all threads), for launch accounting.
 void note_launches(int n);
 
+// Records a message for vi_last_error() and returns code.
+int set_error(int code, const char* msg);
+
+// Bits of a tile id for `tiles` tiles (the reference's getHigherMsb).
+int tile_bits(size_t tiles);
+
 // Blocks of `threads` threads and `smem` dynamic shared bytes that the current
 // device holds resident at once (SM count x blocks per SM), for persistent
 // grids that loop over their work.
