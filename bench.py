@@ -51,6 +51,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-aabb", action="store_true", help="skip the run with the hashgrid box at the scene bounds")
+    ap.add_argument("--no-gaussians", action="store_true", help="skip the Gaussian front end (extension) measurement")
+    ap.add_argument("--gaussians-only", action="store_true",
+                    help="measure only the Gaussian front end (extension) and print its object (profiling)")
     ap.add_argument("--exact-gradients", action="store_true",
                     help="exact-gradient backward (extension) instead of the reference's formula")
     ap.add_argument("--views", default="one", choices=["one", "all"],
@@ -240,6 +243,11 @@ def run_ours(args):
     import volume_integration as vi
     from volume_integration import _C
     from volume_integration.distributed import allreduce_gradients
+    if args.gaussians_only:
+        flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)  # > 126 MB L2
+        if rank == 0:
+            print(json.dumps(run_gaussians(args, flush, device)), flush=True)
+        return
 
     means, conf, views, total_views = workload(args.config, rank, world, device, args.views == "all")
     if args.exact_gradients:
@@ -352,6 +360,9 @@ def run_ours(args):
         line["scene_bounds"] = run_scene_bounds(args, step, means, leaves, views, total_views, flush, world, dist,
                                                 device, _C)
 
+    if world == 1 and not args.no_gaussians:
+        line["gaussians"] = run_gaussians(args, flush, device)
+
     if not args.no_e2e:
         line["e2e"] = run_e2e(args, vi, means, conf, views, total_views, world, dist if world > 1 else None, device)
 
@@ -400,6 +411,73 @@ def run_scene_bounds(args, step, means, leaves, views, total_views, flush, world
     return {"value": round(total_views * steps / (total_ms / 1000.0), 3), "unit": "frames/s", "steps": steps,
             "ms_per_step": round(total_ms / steps, 4), "hash_bounds": [round(v, 4) for v in lo + hi],
             "stage_ms_per_step": {k: round(v[0] / steps, 4) for k, v in prof.items()}}
+
+
+def run_gaussians(args, flush, device):
+    """The Gaussian front end (extension) on the scene's Gaussian attributes (SH
+    degree 3): preprocess forward, its backward and the tile binning per step,
+    each timed with CUDA events on the launching stream."""
+    import vi_workloads as wl
+    import volume_integration.gaussians as vg
+    peak, peak_kind = measured_peaks()
+    means, scales, q, opac, shs, cam = wl.gaussians(args.config)
+    P = means.shape[0]
+    leaves = [t.to(device).requires_grad_(True) for t in (means, scales, q, opac, shs)]
+    gc = vg.GaussianCamera(image_height=cam["image_height"], image_width=cam["image_width"],
+                           tanfovx=cam["tanfovx"], tanfovy=cam["tanfovy"], viewmatrix=cam["viewmatrix"].to(device),
+                           projmatrix=cam["projmatrix"].to(device), campos=cam["cam_pos"].to(device), sh_degree=3)
+    gen = torch.Generator().manual_seed(5)
+    grads = [torch.randn(P, 2, generator=gen).to(device), torch.randn(P, generator=gen).to(device),
+             torch.zeros(P, 6, device=device), torch.randn(P, 4, generator=gen).to(device),
+             torch.randn(P, 3, generator=gen).to(device)]
+    W, H = cam["image_width"], cam["image_height"]
+
+    stats = {}
+
+    def one(ev=None):
+        if ev: ev[0].record()
+        out = vg.preprocess_gaussians(*leaves, gc)
+        if ev: ev[1].record()
+        g = torch.autograd.grad((out.means2D, out.depths, out.cov3D, out.conic_opacity, out.rgb), leaves, grads)
+        if ev: ev[2].record()
+        bins = vg.bin_gaussians(out, W, H)
+        if ev: ev[3].record()
+        stats["R"], stats["radii"] = bins.point_list.numel(), out.radii
+        # results are dropped here, so the next step reuses their memory (the
+        # warm-up steps grow torch's caching allocator to the step's peak)
+    for _ in range(max(10, args.warmup)):
+        one()
+    torch.cuda.synchronize()
+    steps = max(1, min(args.steps, 50))
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
+    for i in range(steps):
+        flush.zero_()
+        one(evs[i])
+    torch.cuda.synchronize()
+    fwd = sum(e[0].elapsed_time(e[1]) for e in evs) / steps
+    bwd = sum(e[1].elapsed_time(e[2]) for e in evs) / steps
+    binning = sum(e[2].elapsed_time(e[3]) for e in evs) / steps
+    R = int(stats["R"])
+    visible = int((stats["radii"] > 0).sum())
+    # algorithmic bytes per Gaussian: forward reads means, scales, rotation, opacity and
+    # 16x3 SH floats (236 B) and writes radii, means2D, depth, cov3D, conic+opacity,
+    # rgb, clamped flags and tiles touched (75 B); the backward reads the inputs but the
+    # opacity, radii, clamped flags and 64 B of incoming gradients (303 B) and writes
+    # the gradients of means, scales, rotation and SH (232 B)
+    fwd_bytes, bwd_bytes = 311 * P, 535 * P
+    ach = fwd_bytes / (fwd / 1000.0) / 1e9
+    ach_b = bwd_bytes / (bwd / 1000.0) / 1e9
+    return {"value": round(P / ((fwd + bwd) / 1000.0), 1), "unit": "Gaussians/s (preprocess forward+backward)",
+            "workload": f"{args.config}: {P} Gaussians, SH degree 3, {W}x{H}",
+            "steps": steps, "preprocess_ms": round(fwd, 4), "backward_ms": round(bwd, 4),
+            "binning_ms": round(binning, 4), "visible": visible, "num_rendered": R,
+            "binning_keys_per_s": round(R / (binning / 1000.0), 1) if binning > 0 else None,
+            "roofline": {"bound": "hbm", "kernel": "gauss_preprocess_kernel", "achieved": round(ach, 1),
+                         "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4), "peak_kind": peak_kind,
+                         "algorithmic_bytes": fwd_bytes},
+            "roofline_backward": {"bound": "hbm", "kernel": "gauss_backward_kernel", "achieved": round(ach_b, 1),
+                                  "peak": peak, "unit": "GB/s", "frac": round(ach_b / peak, 4),
+                                  "algorithmic_bytes": bwd_bytes}}
 
 
 def run_e2e(args, vi, means, conf, views, total_views, world, dist, device):

@@ -255,6 +255,7 @@ Tensor aligned16(const Tensor& t) {
   return c;
 }
 
+// The camera position by value (a device tensor costs a blocking copy).
 std::vector<float> host3(const Tensor& t) {
   Tensor h = t.detach().to(torch::kCPU, torch::kFloat32).contiguous().view({-1});
   TORCH_CHECK(h.numel() == 3, "campos must hold 3 values");

@@ -214,30 +214,38 @@ __device__ __forceinline__ bool gauss_geometry(const GaussCam& cm, float3 p, flo
   return true;
 }
 
-// Stages `count` floats starting at src (16-byte aligned when count_per * first
-// is a multiple of 4) into shared memory with coalesced loads.
-__device__ __forceinline__ void stage_in(float* dst, const float* __restrict__ src, int count) {
-  const bool vec = (((uintptr_t)src) & 15u) == 0;
-  if (vec) {
-    const int n4 = count >> 2;
-    const float4* s4 = reinterpret_cast<const float4*>(src);
-    float4* d4 = reinterpret_cast<float4*>(dst);
-    for (int i = threadIdx.x; i < n4; i += blockDim.x) d4[i] = __ldg(s4 + i);
-    for (int i = (n4 << 2) + threadIdx.x; i < count; i += blockDim.x) dst[i] = __ldg(src + i);
+// Shared-memory row stride (floats) of one Gaussian's `per` SH floats: odd, so
+// the threads of a warp, each reading its own row element by element, hit
+// distinct banks (a stride of 48 would put 16 threads on each bank).
+__host__ __device__ inline int sh_stride(int per) { return per | 1; }
+
+// Stages the block's n rows of `per` floats (contiguous at src) into padded
+// shared rows with coalesced global loads (16-byte when the rows allow it).
+__device__ __forceinline__ void stage_in(float* dst, const float* __restrict__ src, int n, int per, int stride) {
+  const int count = n * per;
+  if ((((uintptr_t)src) & 15u) == 0 && per % 4 == 0) {
+    const float4* g4 = reinterpret_cast<const float4*>(src);
+    for (int i = threadIdx.x; i < (count >> 2); i += blockDim.x) {
+      const float4 v = __ldg(g4 + i);
+      const int e = 4 * i, row = e / per;
+      float* d = dst + row * stride + (e - row * per);
+      d[0] = v.x; d[1] = v.y; d[2] = v.z; d[3] = v.w;
+    }
   } else {
-    for (int i = threadIdx.x; i < count; i += blockDim.x) dst[i] = __ldg(src + i);
+    for (int i = threadIdx.x; i < count; i += blockDim.x) dst[(i / per) * stride + i % per] = __ldg(src + i);
   }
 }
-__device__ __forceinline__ void stage_out(float* __restrict__ dst, const float* src, int count) {
-  const bool vec = (((uintptr_t)dst) & 15u) == 0;
-  if (vec) {
-    const int n4 = count >> 2;
-    const float4* s4 = reinterpret_cast<const float4*>(src);
-    float4* d4 = reinterpret_cast<float4*>(dst);
-    for (int i = threadIdx.x; i < n4; i += blockDim.x) d4[i] = s4[i];
-    for (int i = (n4 << 2) + threadIdx.x; i < count; i += blockDim.x) dst[i] = src[i];
+__device__ __forceinline__ void stage_out(float* __restrict__ dst, const float* src, int n, int per, int stride) {
+  const int count = n * per;
+  if ((((uintptr_t)dst) & 15u) == 0 && per % 4 == 0) {
+    float4* g4 = reinterpret_cast<float4*>(dst);
+    for (int i = threadIdx.x; i < (count >> 2); i += blockDim.x) {
+      const int e = 4 * i, row = e / per;
+      const float* s = src + row * stride + (e - row * per);
+      g4[i] = make_float4(s[0], s[1], s[2], s[3]);
+    }
   } else {
-    for (int i = threadIdx.x; i < count; i += blockDim.x) dst[i] = src[i];
+    for (int i = threadIdx.x; i < count; i += blockDim.x) dst[i] = src[(i / per) * stride + i % per];
   }
 }
 
@@ -253,8 +261,8 @@ __global__ void __launch_bounds__(kGaussThreads) gauss_preprocess_kernel(
   float* sh_s = reinterpret_cast<float*>(sh_smem4);
   const int i0 = blockIdx.x * kGaussThreads;
   const int n = min(kGaussThreads, P - i0);
-  const int per = cm.M * 3;
-  stage_in(sh_s, shs + (size_t)i0 * per, n * per);
+  const int per = cm.M * 3, stride = sh_stride(per);
+  stage_in(sh_s, shs + (size_t)i0 * per, n, per, stride);
   __syncthreads();
   const int i = i0 + (int)threadIdx.x;
   if (i >= P) return;
@@ -296,7 +304,7 @@ __global__ void __launch_bounds__(kGaussThreads) gauss_preprocess_kernel(
   float Y[kMaxShCoeffs];
   sh_basis(x, y, z, cm.deg, Y);
   const int nb = (cm.deg + 1) * (cm.deg + 1);
-  const float* sh = sh_s + threadIdx.x * per;
+  const float* sh = sh_s + threadIdx.x * stride;
   float col[3] = {0.f, 0.f, 0.f};
 #pragma unroll
   for (int k = 0; k < kMaxShCoeffs; k++) {
@@ -326,7 +334,7 @@ __global__ void __launch_bounds__(kGaussThreads) gauss_preprocess_kernel(
 // conic (x, y, z of conic_opacity) and rgb with respect to means3D, scales,
 // rotations and shs.  The SH gradients leave through shared memory with
 // coalesced 16-byte stores.
-__global__ void __launch_bounds__(kGaussThreads) gauss_backward_kernel(
+__global__ void __launch_bounds__(kGaussThreads, 5) gauss_backward_kernel(
     int P, GaussCam cm, const float* __restrict__ means3D, const float* __restrict__ scales,
     const float* __restrict__ rotations, const float* __restrict__ shs, const int* __restrict__ radii,
     const uint8_t* __restrict__ clamped, const float* __restrict__ dL_dmeans2D, const float* __restrict__ dL_ddepths,
@@ -337,11 +345,11 @@ __global__ void __launch_bounds__(kGaussThreads) gauss_backward_kernel(
   float* sh_s = reinterpret_cast<float*>(sh_smem4);
   const int i0 = blockIdx.x * kGaussThreads;
   const int n = min(kGaussThreads, P - i0);
-  const int per = cm.M * 3;
-  stage_in(sh_s, shs + (size_t)i0 * per, n * per);
+  const int per = cm.M * 3, stride = sh_stride(per);
+  stage_in(sh_s, shs + (size_t)i0 * per, n, per, stride);
   __syncthreads();
   const int i = i0 + (int)threadIdx.x;
-  float* dsh = sh_s + threadIdx.x * per;  // this Gaussian's coefficients, then their gradients
+  float* dsh = sh_s + threadIdx.x * stride;  // this Gaussian's coefficients, then their gradients
   bool live = i < P && radii[i] > 0;
   float3 dp = make_float3(0.f, 0.f, 0.f);
   float dsc[3] = {0.f, 0.f, 0.f}, dq[4] = {0.f, 0.f, 0.f, 0.f};
@@ -497,7 +505,7 @@ __global__ void __launch_bounds__(kGaussThreads) gauss_backward_kernel(
     reinterpret_cast<float4*>(dL_drotations)[i] = make_float4(dq[0], dq[1], dq[2], dq[3]);
   }
   __syncthreads();
-  stage_out(dL_dshs + (size_t)i0 * per, sh_s, n * per);
+  stage_out(dL_dshs + (size_t)i0 * per, sh_s, n, per, stride);
 }
 
 __global__ void __launch_bounds__(256) gauss_depth_keys_kernel(int P, const float* __restrict__ depths,
@@ -578,7 +586,7 @@ extern "C" int vi_preprocess_gaussians(int P, int sh_degree, int sh_coeffs, cons
   if (((uintptr_t)rotations & 15u) || ((uintptr_t)conic_opacity & 15u))
     return gfail(VI_ERR_INVALID_ARGUMENT, "vi_preprocess_gaussians: rotations and conic_opacity must be 16-byte aligned");
   host_camera(cm, cam_pos_host, tan_fovx, tan_fovy);
-  const size_t smem = sizeof(float) * (size_t)kGaussThreads * sh_coeffs * 3;
+  const size_t smem = sizeof(float) * (size_t)kGaussThreads * sh_stride(sh_coeffs * 3);
   cudaFuncSetAttribute(gauss_preprocess_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   gauss_preprocess_kernel<<<(P + kGaussThreads - 1) / kGaussThreads, kGaussThreads, smem, (cudaStream_t)stream>>>(
       P, cm, means3D, scales, rotations, opacities, shs, radii, means2D, depths, cov3D, conic_opacity, rgb, clamped,
@@ -607,7 +615,7 @@ extern "C" int vi_preprocess_gaussians_backward(
   if (((uintptr_t)rotations & 15u) || ((uintptr_t)dL_drotations & 15u))
     return gfail(VI_ERR_INVALID_ARGUMENT, "vi_preprocess_gaussians_backward: rotations must be 16-byte aligned");
   host_camera(cm, cam_pos_host, tan_fovx, tan_fovy);
-  const size_t smem = sizeof(float) * (size_t)kGaussThreads * sh_coeffs * 3;
+  const size_t smem = sizeof(float) * (size_t)kGaussThreads * sh_stride(sh_coeffs * 3);
   cudaFuncSetAttribute(gauss_backward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   gauss_backward_kernel<<<(P + kGaussThreads - 1) / kGaussThreads, kGaussThreads, smem, (cudaStream_t)stream>>>(
       P, cm, means3D, scales, rotations, shs, radii, clamped, dL_dmeans2D, dL_ddepths, dL_dcov3D, dL_dconic_opacity,

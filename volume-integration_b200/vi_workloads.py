@@ -185,3 +185,27 @@ def make(name, table_range=1e-4, seed=None, **over):
     )
     kw.update({k: v for k, v in hg.items()})
     return means, conf, kw, cams
+
+
+def gaussians(name="headline", seed=None, sh_degree=3):
+    """Seeded Gaussian attributes of a scene's shape (the Gaussian front end's workload).
+
+    Centres as ``make(name)``; log-normal scales per axis (mu = the scene's
+    mu_scale, sigma 0.7); random unit quaternions (r, x, y, z); opacity
+    sigmoid(N(0, 1)); SH coefficients N(0, 0.2) of the given degree.  Returns
+    (means3D, scales, rotations, opacities [P, 1], shs [P, (deg+1)^2, 3], camera).
+    """
+    c = dict(CONFIGS[name])
+    gen = torch.Generator().manual_seed((SEEDS.get(name, 999) if seed is None else seed) + 7)
+    P = c["P"]
+    if c["layout"] == "box":
+        means = (torch.rand(P, 3, generator=gen) * 2 - 1) * c["extent"]
+    else:
+        means = mixture(P, c["clusters"], c["extent"], gen)
+    scales = torch.exp(c["mu_scale"] + 0.7 * torch.randn(P, 3, generator=gen))
+    q = torch.randn(P, 4, generator=gen)
+    q = q / q.norm(dim=1, keepdim=True)
+    opac = torch.sigmoid(torch.randn(P, 1, generator=gen))
+    shs = 0.2 * torch.randn(P, (sh_degree + 1) ** 2, 3, generator=gen)
+    cam = camera((0.0, 0.0, -c["dist"]), c["width"], c["height"], c["fov"])
+    return means, scales, q, opac, shs, cam

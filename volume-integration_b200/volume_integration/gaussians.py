@@ -29,7 +29,8 @@ class GaussianCamera:
 
     ``viewmatrix`` is world->view transposed and ``projmatrix`` is
     (proj @ view) transposed, both stored row-major (as ``IntegrationSettings``);
-    ``campos`` is the camera centre.
+    ``campos`` is the camera centre, kept on the host (the kernels take it by
+    value, so a device tensor is copied once here rather than at every call).
     """
     image_height: int
     image_width: int
@@ -41,6 +42,9 @@ class GaussianCamera:
     sh_degree: int = 3
     scale_modifier: float = 1.0
     near_plane: float = 0.2
+
+    def __post_init__(self):
+        self.campos = torch.as_tensor(self.campos).detach().to("cpu", torch.float32).reshape(3)
 
 
 class ProjectedGaussians(NamedTuple):
