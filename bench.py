@@ -482,25 +482,43 @@ def run_gaussians(args, flush, device):
 
 def run_e2e(args, vi, means, conf, views, total_views, world, dist, device):
     """Same step through the public API with host inputs: pinned H2D copies of every
-    input (the scene once, dL/dimage per view) and D2H copies of the images and
-    gradients inside the timed region."""
+    input (the scene, and dL/dimage per view) and D2H copies of the images and
+    gradients of every step inside the timed region.
+
+    The steps are pipelined as a training loop's data path would be: step i+1's
+    inputs are copied on a copy stream into the second of two device input sets
+    while step i computes, and step i's results are read back on a third stream
+    while step i+1 computes (results are recorded on that stream, so the caching
+    allocator does not hand their memory out before the read finishes)."""
     from volume_integration.distributed import allreduce_gradients
     s = views[0][0]
     scene = [t.detach().cpu().pin_memory() for t in (means, conf, s.feature_table, s.linear_weights, s.linear_bias)]
     per_view = [[t.detach().cpu().pin_memory() for t in (gc, gf)] for _, gc, gf in views]
-    dev_scene = [torch.empty_like(t, device=device) for t in scene]
-    dev_views = [[torch.empty_like(t, device=device) for t in pv] for pv in per_view]
-    outs = None
+    slots = [([torch.empty_like(t, device=device) for t in scene],
+              [[torch.empty_like(t, device=device) for t in pv] for pv in per_view]) for _ in range(2)]
     h2d = sum(t.numel() * t.element_size() for t in scene) + \
         sum(t.numel() * t.element_size() for pv in per_view for t in pv)
+    comp = torch.cuda.current_stream()
+    copy_s, read_s = torch.cuda.Stream(device=device), torch.cuda.Stream(device=device)
+    h2d_ev = [torch.cuda.Event() for _ in range(2)]
+    done_ev = [torch.cuda.Event() for _ in range(2)]
+    outs = None
 
-    def one():
-        nonlocal outs
-        for d, h in zip(dev_scene, scene):
-            d.copy_(h, non_blocking=True)
-        for dv, pv in zip(dev_views, per_view):
-            for d, h in zip(dv, pv):
+    def load(k):
+        dev_scene, dev_views = slots[k]
+        with torch.cuda.stream(copy_s):
+            copy_s.wait_event(done_ev[k])  # the step that last used this input set has finished
+            for d, h in zip(dev_scene, scene):
                 d.copy_(h, non_blocking=True)
+            for dv, pv in zip(dev_views, per_view):
+                for d, h in zip(dv, pv):
+                    d.copy_(h, non_blocking=True)
+            h2d_ev[k].record(copy_s)
+
+    def compute(k):
+        nonlocal outs
+        dev_scene, dev_views = slots[k]
+        comp.wait_event(h2d_ev[k])
         m, c, t, w, b = dev_scene
         for x in (c, t, w, b):
             x.requires_grad_(True)
@@ -512,22 +530,34 @@ def run_e2e(args, vi, means, conf, views, total_views, world, dist, device):
             res += [oc.detach(), of.detach(), vis.detach()]
         allreduce_gradients(acc)
         res += acc
-        if outs is None:
-            outs = [torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res]
-        for o, r in zip(outs, res):
-            o.copy_(r, non_blocking=True)
         for x in (c, t, w, b):
             x.requires_grad_(False)
+        done_ev[k].record(comp)
+        if outs is None:
+            outs = [torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res]
+        with torch.cuda.stream(read_s):
+            read_s.wait_event(done_ev[k])
+            for o, r in zip(outs, res):
+                r.record_stream(read_s)
+                o.copy_(r, non_blocking=True)
 
-    for _ in range(max(1, args.warmup)):
-        one()
+    def run(n):
+        load(0)
+        for i in range(n):
+            if i + 1 < n:
+                load((i + 1) % 2)
+            compute(i % 2)
+        comp.wait_stream(read_s)
+        comp.wait_stream(copy_s)
+
+    run(max(2, args.warmup))
     torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
-    for _ in range(args.steps):
-        one()
+    copy_s.wait_stream(comp)  # the first copy starts inside the timed region
+    run(args.steps)
     b.record()
     torch.cuda.synchronize()
     ms = a.elapsed_time(b)
@@ -537,7 +567,8 @@ def run_e2e(args, vi, means, conf, views, total_views, world, dist, device):
         ms = float(t.item())
     d2h = sum(o.numel() * o.element_size() for o in outs)
     return {"value": round(total_views * args.steps / (ms / 1000.0), 3), "unit": "frames/s",
-            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)}
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+            "pipelined": "inputs of step i+1 copied and results of step i read back while step i / i+1 compute"}
 
 
 # ---------------------------------------------------------------------------
