@@ -69,6 +69,49 @@ def test_custom(name):
     _check(means, conf, s, seed=3)
 
 
+def _projection_crossings(s, n=4_000_000, seed=0):
+    """World points (float32) whose pixel under the forward's 1/(w + 1e-7)
+    projection differs from the backward's 1/w one (forward.cu:432,
+    backward.cu:325), found by sampling the view at depths 0.25-0.6 with the
+    kernels' float32 operation order."""
+    f32 = np.float32
+    W, H = s.image_width, s.image_height
+    pm = s.projmatrix.cpu().numpy().reshape(16).astype(np.float32)
+    vm = s.viewmatrix.cpu().numpy().reshape(16).astype(np.float32)
+    eye = s.cam_pos.cpu().numpy().astype(np.float64)
+    rows = np.array([[vm[0], vm[4], vm[8]], [vm[1], vm[5], vm[9]], [vm[2], vm[6], vm[10]]], np.float64)
+    rng = np.random.default_rng(seed)
+    d = rng.uniform(0.25, 0.6, n)
+    cam = np.stack([rng.uniform(-1, 1, n) * d * s.tanfovx, rng.uniform(-1, 1, n) * d * s.tanfovy, d], 1)
+    p = (eye[None, :] + cam @ rows).astype(np.float32)
+
+    def pixel(fwd):
+        hx = ((pm[0] * p[:, 0] + pm[4] * p[:, 1]) + pm[8] * p[:, 2]) + pm[12]
+        hy = ((pm[1] * p[:, 0] + pm[5] * p[:, 1]) + pm[9] * p[:, 2]) + pm[13]
+        hw = ((pm[3] * p[:, 0] + pm[7] * p[:, 1]) + pm[11] * p[:, 2]) + pm[15]
+        pw = f32(1) / (hw + f32(1e-7)) if fwd else f32(1) / hw
+        n2p = lambda q, S: (((q.astype(np.float64) + 1) * S - 1) * 0.5).astype(np.float32)
+        return np.floor(n2p(hx * pw, W)), np.floor(n2p(hy * pw, H))
+    (ax, ay), (bx, by) = pixel(True), pixel(False)
+    return p[(ax != bx) | (ay != by)]
+
+
+def test_backward_recompute_of_records_whose_projection_differs():
+    # Primitives centred on points that the backward's 1/w projection puts in
+    # another pixel than the forward's 1/(w + 1e-7): their records are
+    # re-derived before the per-pixel pass (recompute_records_kernel), and the
+    # gradients must match the oracle's backward, which recomputes them too.
+    means, conf, s = tl.custom_scene(seed=41, P=300, W=256, H=256, fov=90.0, dist=0.05, extent=0.4, scale=0.05,
+                                     mu_conf=1.5)
+    pts = _projection_crossings(s)
+    assert len(pts) >= 20
+    means = means.clone()
+    means[:20] = torch.from_numpy(pts[:20]).to(means.device)
+    g, o = _check(means, conf, s, seed=5)
+    flagged = (g["rec_cnt"].view(np.uint32) >> 31) & 1
+    assert flagged[:20].sum() >= 10, flagged[:20]
+
+
 def test_single_primitive():
     means, conf, s = tl.custom_scene(P=1, scale=0.8, mu_conf=2.0)
     g, o = _check(means, conf, s)

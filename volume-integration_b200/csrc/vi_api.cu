@@ -147,6 +147,7 @@ GeomState geom_layout(char* base, size_t P, int V, int O, int D) {
   g.rec_dpre = c.take<float>(P * V * OP);
   char* st = c.take<char>(sort_temp_bytes(P, 4, 0, 32));
   sort_temp_carve(st, P, 4, 0, 32, g.sort);
+  g.differs_list = c.take<uint32_t>(P);
   // Last, so the offsets above do not depend on D.
   g.cls_base = c.take<uint32_t>(P);
   const size_t want = P * (size_t)V;

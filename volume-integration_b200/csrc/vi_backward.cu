@@ -9,8 +9,9 @@
 //     backward.cu:771-778) and writes dL/d(pre-activation) of each contributing
 //     (primitive, pixel) record.  Blend and density come from the forward record
 //     (identical to the reference's recompute when the forward and backward
-//     projections put every grid point in the same pixel; otherwise the
-//     record is recomputed with the backward projection).
+//     projections put every grid point in the same pixel; the records of the
+//     other primitives are recomputed with the backward projection first, by
+//     recompute_records_kernel, from a list the feature stage keeps).
 //  2. backward_prim: one warp per primitive, lane = grid point, gathers its
 //     contributing records and produces (hashgrid work once per distinct
 //     normalised position of the primitive's grid points)
@@ -109,7 +110,7 @@ __global__ void __launch_bounds__(256) backward_pixel_kernel(Scene sc, GeomState
   const int K = sc.K;
   int nc = min(im.n_contrib[pix], K);
   if (nc <= 0) return;
-  const int O = sc.O, B = O - 1, Fout = sc.Fout, V = sc.V;
+  const int O = sc.O, B = O - 1, Fout = sc.Fout;
   float dOut[OMAX - 1], after[OMAX - 1];
 #pragma unroll
   for (int d = 0; d < OMAX - 1; d++) {
@@ -125,7 +126,6 @@ __global__ void __launch_bounds__(256) backward_pixel_kernel(Scene sc, GeomState
 #pragma unroll
   for (int f = 0; f < OMAX - 4; f++)
     if (f < Fout) dOut[3 + f] = dL_dfeat ? dL_dfeat[f * N + pix] : 0.0f;
-  const int px = (int)(pix % sc.W), py = (int)(pix / sc.W);
   // Contributors are visited in reverse; the record slot, delta t and
   // properties of the next one are loaded while the current one is processed.
   const uint32_t* crec = im.contrib_rec + pix * K;
@@ -153,7 +153,6 @@ __global__ void __launch_bounds__(256) backward_pixel_kernel(Scene sc, GeomState
 #pragma unroll
       for (int o4 = 0; o4 < OMAX / 4; o4++) pn[o4] = src[o4];
     }
-    if (r & kBwdDiffers) recompute_props<OMAX>(sc, rec / V, px, py, props);
     float dens = 0.0f;
 #pragma unroll
     for (int o = 0; o < OMAX; o++)
@@ -935,6 +934,30 @@ void launch_prim_t(const Scene& sc, GeomState& g, float* dmeans, float* dconf, f
   note_launches(1);
 }
 
+// Properties of the records of primitives whose backward projection puts a
+// grid point in another pixel than the forward's (kBwdDiffers, listed by the
+// feature stage), re-derived as the reference's backward does
+// (backward.cu:404-569) and written over the forward's rec_props, which the
+// render has consumed.  One thread per (listed primitive, record slot); the
+// per-pixel pass then reads rec_props alone.
+template <int OMAX>
+__global__ void __launch_bounds__(128) recompute_records_kernel(Scene sc, GeomState g) {
+  const uint32_t n_list = g.status[7];
+  const uint32_t V = (uint32_t)sc.V;
+  for (uint64_t t = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; t < (uint64_t)n_list * V;
+       t += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t q = g.differs_list[t / V], j = (uint32_t)(t % V);
+    if (j >= (g.rec_cnt[q] & ~kBwdDiffers)) continue;
+    const size_t slot = (size_t)q * V + j;
+    const uint32_t key = g.rec_key[slot], tile = key >> 8;
+    const int px = (int)((tile % sc.gx) * VI_TILE + (key & 15u)), py = (int)((tile / sc.gx) * VI_TILE + ((key >> 4) & 15u));
+    float props[OMAX];
+    recompute_props<OMAX>(sc, q, px, py, props);
+#pragma unroll
+    for (int o = 0; o < OMAX; o++) g.rec_props[slot * OMAX + o] = props[o];
+  }
+}
+
 }  // namespace
 
 void launch_backward(const Scene& sc, GeomState& g, const ImgState& im, const uint32_t* point_list,
@@ -944,6 +967,13 @@ void launch_backward(const Scene& sc, GeomState& g, const ImgState& im, const ui
   cudaMemsetAsync(g.rec_pix, 0, (size_t)sc.P * sc.V * sizeof(uint32_t), s);
   const bool o16 = sc.O > 8;
   stage_begin(kStBwdPixel, s);
+  if (!sc.exact && sc.P > 0) {  // the exact mode differentiates the forward's properties
+    if (o16)
+      recompute_records_kernel<16><<<148 * 4, 128, 0, s>>>(sc, g);
+    else
+      recompute_records_kernel<8><<<148 * 4, 128, 0, s>>>(sc, g);
+    note_launches(1);
+  }
   if (N > 0) {
     note_launches(1);
     const unsigned blocks = (unsigned)((N + 255) / 256);

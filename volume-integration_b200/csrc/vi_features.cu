@@ -265,6 +265,8 @@ __global__ void __launch_bounds__(kFeatWarps * 32, 3) features_kernel(Scene sc, 
     if (lane == 0) {
       g.rec_cnt[q] = (uint32_t)__popc(recmask) | (differs ? kBwdDiffers : 0u);
       g.cls_base[q] = cbase;
+      // the backward re-derives these records' properties with its own projection
+      if (differs && recmask) g.differs_list[atomicAdd(g.status + 7, 1u)] = (uint32_t)q;
     }
     __syncwarp();
     }

@@ -55,7 +55,7 @@ bool onesweep_sort_u64(uint64_t* keys, uint32_t* vals, uint64_t* alt_keys, uint3
 // Geometry state: everything sized by the primitive count P.
 // ---------------------------------------------------------------------------
 struct GeomState {
-  uint32_t* status;          // [0] status bits, [2..3] num_rendered as u64, [4] feature-stage chunk counter, [5] backward work counter, [6] phi_cache slots used
+  uint32_t* status;          // [0] status bits, [2..3] num_rendered as u64, [4] feature-stage chunk counter, [5] backward work counter, [6] phi_cache slots used, [7] entries of differs_list
   float* depths;             // [P] view-space z of the centre
   int* radii;                // [P]
   float* means2D;            // [2P]
@@ -72,6 +72,7 @@ struct GeomState {
   uint32_t* rec_pix;         // [P*V] pixel + 1 of a contributing record, 0 otherwise (backward)
   float* rec_dpre;           // [P*V*O] dL/d(pre-activation) per contributing record
   SortTemp sort;
+  uint32_t* differs_list;    // [P] primitives with records whose backward projection differs (kBwdDiffers)
   uint32_t* cls_base;        // [P] first slot of the primitive's position classes in phi_cache, or kNoCache
   float* phi_cache;          // [phi_cap][D] hashgrid features of each position class (feature stage)
   uint32_t phi_cap;          // slots in phi_cache
