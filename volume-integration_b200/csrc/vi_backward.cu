@@ -17,12 +17,13 @@
 //     normalised position of the primitive's grid points)
 //       dconf[q,g]  = sum_p (dIn_p . phi_g) * g'_{p,g}                (backward.cu:697-710)
 //       dtable      += (sum_p dIn_p * g'_{p,g} * conf_g) * corner weight (hashgrid.h:43-95)
-//       dW, db      += dpre_p (x) in_p, dpre_p                          (backward.cu:621-641)
+//       dW          += dpre_p (x) in_p                                  (backward.cu:621-641)
 //     where g' is the stencil magnitude of "neighbour's screen point lies in
 //     pixel p" (backward.cu:644-689).  The table scatter is linear in dIn, so
 //     each position class scatters once per level and corner instead of once
 //     per pixel and grid point; its features come from the feature stage's
-//     cache.  dW/db are reduced per CTA before global atomics.
+//     cache.  dW is reduced per CTA before global atomics; db = sum_p dpre_p is
+//     summed by the per-pixel pass, which writes every dpre_p once.
 //
 // With the exact-gradient flag both kernels compute the derivative of the
 // forward instead (backward_pixel_exact_kernel, backward_prim_kernel<.., true>).
@@ -100,16 +101,44 @@ __device__ __noinline__ void recompute_props(const Scene& sc, uint32_t q, int px
   }
 }
 
+// dL/db = the sum of dL/dpre over every contributing record (backward.cu:
+// 621-641); each record is written by exactly one pixel, so the per-pixel pass
+// sums it: per thread, then per warp by shuffles and per block in shared
+// memory, then one atomic per output and block.  Called by every thread of a
+// 256-thread block.
+template <int OMAX>
+__device__ __forceinline__ void block_add_db(const float* dbl, int O, float* __restrict__ db) {
+  __shared__ float part[8][OMAX];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 0; o < OMAX; o++) {
+    float x = dbl[o];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) x += __shfl_xor_sync(0xffffffffu, x, off);
+    if (lane == 0) part[w][o] = x;
+  }
+  __syncthreads();
+  if ((int)threadIdx.x < O) {
+    float x = 0.0f;
+#pragma unroll
+    for (int ww = 0; ww < 8; ww++) x += part[ww][threadIdx.x];
+    if (x != 0.0f) atomicAdd(&db[threadIdx.x], x);
+  }
+}
+
 template <int OMAX>
 __global__ void __launch_bounds__(256) backward_pixel_kernel(Scene sc, GeomState g, ImgState im,
                                                             const float* __restrict__ dL_dcolor,
-                                                            const float* __restrict__ dL_dfeat) {
+                                                            const float* __restrict__ dL_dfeat,
+                                                            float* __restrict__ db) {
   const size_t N = (size_t)sc.W * sc.H;
   const size_t pix = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
-  if (pix >= N) return;
+  float dbl[OMAX];
+#pragma unroll
+  for (int o = 0; o < OMAX; o++) dbl[o] = 0.0f;
   const int K = sc.K;
-  int nc = min(im.n_contrib[pix], K);
-  if (nc <= 0) return;
+  const int nc = pix < N ? min(im.n_contrib[pix], K) : 0;
+  if (nc > 0) {
   const int O = sc.O, B = O - 1, Fout = sc.Fout;
   float dOut[OMAX - 1], after[OMAX - 1];
 #pragma unroll
@@ -177,6 +206,8 @@ __global__ void __launch_bounds__(256) backward_pixel_kernel(Scene sc, GeomState
     for (int o4 = 0; o4 < OMAX / 4; o4++) dst[o4] = make_float4(dpre[4 * o4], dpre[4 * o4 + 1], dpre[4 * o4 + 2], dpre[4 * o4 + 3]);
     g.rec_pix[rec] = (uint32_t)pix + 1u;
 #pragma unroll
+    for (int o = 0; o < OMAX; o++) dbl[o] += dpre[o];
+#pragma unroll
     for (int d = 0; d < OMAX - 1; d++) {
       if (d < B) {
         const float y = props[d];
@@ -185,6 +216,8 @@ __global__ void __launch_bounds__(256) backward_pixel_kernel(Scene sc, GeomState
       }
     }
   }
+  }
+  block_add_db<OMAX>(dbl, sc.O, db);
 }
 
 // Exact-gradient mode, per pixel: the derivative of the forward's compositing
@@ -205,13 +238,16 @@ __global__ void __launch_bounds__(256) backward_pixel_exact_kernel(Scene sc, Geo
                                                                   const float* __restrict__ dL_dcolor,
                                                                   const float* __restrict__ dL_dfeat,
                                                                   const float* __restrict__ dL_dvis,
-                                                                  float* __restrict__ dmeans) {
+                                                                  float* __restrict__ dmeans,
+                                                                  float* __restrict__ db) {
   const size_t N = (size_t)sc.W * sc.H;
   const size_t pix = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
-  if (pix >= N) return;
+  float dbl[OMAX];
+#pragma unroll
+  for (int o = 0; o < OMAX; o++) dbl[o] = 0.0f;
   const int K = sc.K;
-  const int nc = min(im.n_contrib[pix], K);
-  if (nc <= 0) return;
+  const int nc = pix < N ? min(im.n_contrib[pix], K) : 0;
+  if (nc > 0) {
   const int O = sc.O, B = O - 1, Fout = sc.Fout, V = sc.V;
   const uint32_t* crec = im.contrib_rec + pix * K;
   const float* cdt = im.delta_t + pix * K;
@@ -292,6 +328,8 @@ __global__ void __launch_bounds__(256) backward_pixel_exact_kernel(Scene sc, Geo
 #pragma unroll
     for (int o4 = 0; o4 < OMAX / 4; o4++) dst[o4] = make_float4(dpre[4 * o4], dpre[4 * o4 + 1], dpre[4 * o4 + 2], dpre[4 * o4 + 3]);
     g.rec_pix[rec] = (uint32_t)pix + 1u;
+#pragma unroll
+    for (int o = 0; o < OMAX; o++) dbl[o] += dpre[o];
     // delta t = depth(trigger) - depth(this primitive), or max_distance - depth
     if (dLddt != 0.0f) {
       const uint32_t q = rec / V;
@@ -311,6 +349,8 @@ __global__ void __launch_bounds__(256) backward_pixel_exact_kernel(Scene sc, Geo
       if (d < B) A[d] = a * props[d] + (1.0f - a) * A[d];
     Vp *= 1.0f - a;
   }
+  }
+  block_add_db<OMAX>(dbl, sc.O, db);
 }
 
 template <int F>
@@ -333,15 +373,15 @@ constexpr int kBwdWarps = 4;
 __host__ __device__ inline int pad4(int x) { return (x + 3) & ~3; }
 __host__ __device__ inline int bwd_dp(int D) { return pad4(D) + 4; }
 // Shared memory of backward_prim_kernel.  Head: W [OMAX][DP] (rows of the
-// linear layer), db [OMAX] partial sums of the CTA, level resolution / hash
-// flag [L].  Per warp: phi [32][DP] (features of each position class), two lane
+// linear layer), level resolution / hash flag [L], box-corner features [8][DP]
+// and coefficients [8][OMAX].  Per warp: phi [32][DP] (features of each position class), two lane
 // rows [32][OMAX] (conf * vA and E of each grid point; the first later holds W
 // phi of each class), two class rows [32][OMAX] (their sums per class; the first
 // stages the records' dL/dpre before that), class positions [32] float4, class
 // member masks [32] and the warp's dW partial sums [OMAX][D] (lane j owns
 // columns j, j + 32).
 __host__ __device__ inline int bwd_head_floats(int D, int L, int OMAX) {
-  return OMAX * bwd_dp(D) + OMAX + 3 * pad4(L) + 8 * bwd_dp(D) + 8 * OMAX;
+  return OMAX * bwd_dp(D) + 3 * pad4(L) + 8 * bwd_dp(D) + 8 * OMAX;
 }
 __host__ __device__ inline int bwd_warp_floats(int D, int OMAX) {
   return 32 * bwd_dp(D) + 4 * 32 * OMAX + 4 * 32 + 32 + OMAX * D;
@@ -469,14 +509,12 @@ __device__ __forceinline__ void scatter_level(const LevelCorners& c, float* __re
 template <int F, int OMAX, bool EXACT>
 __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene sc, GeomState g, float* __restrict__ dmeans,
                                                                       float* __restrict__ dconf,
-                                                                      float* __restrict__ dtable, float* __restrict__ dW,
-                                                                      float* __restrict__ db) {
+                                                                      float* __restrict__ dtable, float* __restrict__ dW) {
   extern __shared__ float4 smem4[];
   float* smem = reinterpret_cast<float*>(smem4);
   const int L = sc.L, D = L * F, DP = bwd_dp(D), O = sc.O, V = sc.V, G = sc.G;
   float* W_s = smem;                                      // [OMAX][DP]
-  float* db_s = W_s + OMAX * DP;                          // [OMAX]
-  float* resf_s = db_s + OMAX;                            // [L]
+  float* resf_s = W_s + OMAX * DP;                        // [L]
   int* res_s = reinterpret_cast<int*>(resf_s + pad4(L));  // [L]
   int* hash_s = res_s + pad4(L);                          // [L]
   float* cphi_s = reinterpret_cast<float*>(hash_s + pad4(L));  // [8][DP] box-corner features
@@ -497,7 +535,6 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
     W_s[i] = o < O && d < D ? sc.Wl[o * D + d] : 0.0f;
   }
   for (int i = (int)(threadIdx.x & 31); i < OMAX * D; i += 32) dWw[i] = 0.0f;
-  for (int i = threadIdx.x; i < OMAX; i += blockDim.x) db_s[i] = 0.0f;
   for (int i = threadIdx.x; i < L; i += blockDim.x) {
     res_s[i] = sc.res[i];
     resf_s[i] = (float)sc.res[i];
@@ -513,7 +550,6 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
   if (!EXACT) box_corner_features<F>(sc, res_s, resf_s, hash_s, p0, p1, p2, DP, cphi_s);
   const uint32_t lt_mask = (1u << lane) - 1u;
   const uint32_t stride = (uint32_t)D;
-  float dbacc = 0.0f;
   // dW column `lane` (the first 32 columns) accumulates in registers; columns
   // 32.. (D > 32) in the warp's shared dWw.
   float dwr[OMAX];
@@ -613,7 +649,6 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
         m &= m - 1;
         const int ppix = (int)__shfl_sync(0xffffffffu, rp, j) - 1;
         if (bpix == ppix) myrec = j;
-        if ((int)lane < O) dbacc += S_s[j * OMAX + lane];
       }
       if (myrec >= 0 && wE != 0.0f) {
         hasE = true;
@@ -632,7 +667,6 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
         m &= m - 1;
         const int ppix = (int)__shfl_sync(0xffffffffu, rp, j) - 1;
         if (bpix == ppix) myrec = j;
-        if ((int)lane < O) dbacc += S_s[j * OMAX + lane];
       }
       if (myrec >= 0 && wE != 0.0f) {
         hasE = true;
@@ -675,7 +709,6 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
         const int j = __ffs(m) - 1;
         m &= m - 1;
         const int ppix = (int)__shfl_sync(0xffffffffu, rp, j) - 1;  // pixel of this contribution
-        if ((int)lane < O) dbacc += S_s[j * OMAX + lane];
         const uint32_t inm = __ballot_sync(0xffffffffu, bpix == ppix);
         if (((inm >> lane) & 1u) && wE != 0.0f) {
           hasE = true;
@@ -885,7 +918,6 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
     for (int o = 0; o < OMAX; o++) dWw[o * D + lane] = dwr[o];
   }
   __syncwarp();
-  if ((int)lane < O && dbacc != 0.0f) atomicAdd(&db_s[lane], dbacc);
   __syncthreads();
   // Table gradient of the box-corner primitives: one scatter per (corner, level).
   for (int t = threadIdx.x; t < 8 * L; t += blockDim.x) {
@@ -913,12 +945,10 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
     for (int ww = 0; ww < kBwdWarps; ww++) x += warp0[(size_t)ww * bwd_warp_floats(D, OMAX) + i];
     if (x != 0.0f) atomicAdd(&dW[i], x);
   }
-  for (int i = threadIdx.x; i < O; i += blockDim.x)
-    if (db_s[i] != 0.0f) atomicAdd(&db[i], db_s[i]);
 }
 
 template <int F, int OMAX>
-void launch_prim_t(const Scene& sc, GeomState& g, float* dmeans, float* dconf, float* dtable, float* dW, float* db,
+void launch_prim_t(const Scene& sc, GeomState& g, float* dmeans, float* dconf, float* dtable, float* dW,
                    cudaStream_t s) {
   const int D = sc.L * F;
   size_t smem = sizeof(float) * (bwd_head_floats(D, sc.L, OMAX) + kBwdWarps * bwd_warp_floats(D, OMAX));
@@ -930,7 +960,7 @@ void launch_prim_t(const Scene& sc, GeomState& g, float* dmeans, float* dconf, f
   const int resident = resident_blocks(reinterpret_cast<const void*>(k), kBwdWarps * 32, smem);
   blocks = blocks < resident ? blocks : resident;
   if (blocks < 1) blocks = 1;
-  k<<<blocks, kBwdWarps * 32, smem, s>>>(sc, g, dmeans, dconf, dtable, dW, db);
+  k<<<blocks, kBwdWarps * 32, smem, s>>>(sc, g, dmeans, dconf, dtable, dW);
   note_launches(1);
 }
 
@@ -979,22 +1009,22 @@ void launch_backward(const Scene& sc, GeomState& g, const ImgState& im, const ui
     const unsigned blocks = (unsigned)((N + 255) / 256);
     if (sc.exact) {
       if (o16)
-        backward_pixel_exact_kernel<16><<<blocks, 256, 0, s>>>(sc, g, im, point_list, dL_dcolor, dL_dfeat, dL_dvis, dmeans);
+        backward_pixel_exact_kernel<16><<<blocks, 256, 0, s>>>(sc, g, im, point_list, dL_dcolor, dL_dfeat, dL_dvis, dmeans, db);
       else
-        backward_pixel_exact_kernel<8><<<blocks, 256, 0, s>>>(sc, g, im, point_list, dL_dcolor, dL_dfeat, dL_dvis, dmeans);
+        backward_pixel_exact_kernel<8><<<blocks, 256, 0, s>>>(sc, g, im, point_list, dL_dcolor, dL_dfeat, dL_dvis, dmeans, db);
     } else if (o16) {
-      backward_pixel_kernel<16><<<blocks, 256, 0, s>>>(sc, g, im, dL_dcolor, dL_dfeat);
+      backward_pixel_kernel<16><<<blocks, 256, 0, s>>>(sc, g, im, dL_dcolor, dL_dfeat, db);
     } else {
-      backward_pixel_kernel<8><<<blocks, 256, 0, s>>>(sc, g, im, dL_dcolor, dL_dfeat);
+      backward_pixel_kernel<8><<<blocks, 256, 0, s>>>(sc, g, im, dL_dcolor, dL_dfeat, db);
     }
   }
   stage_end(kStBwdPixel, s);
   stage_begin(kStBwdPrim, s);
   switch (sc.F) {
-    case 1: o16 ? launch_prim_t<1, 16>(sc, g, dmeans, dconf, dtable, dW, db, s) : launch_prim_t<1, 8>(sc, g, dmeans, dconf, dtable, dW, db, s); break;
-    case 2: o16 ? launch_prim_t<2, 16>(sc, g, dmeans, dconf, dtable, dW, db, s) : launch_prim_t<2, 8>(sc, g, dmeans, dconf, dtable, dW, db, s); break;
-    case 4: o16 ? launch_prim_t<4, 16>(sc, g, dmeans, dconf, dtable, dW, db, s) : launch_prim_t<4, 8>(sc, g, dmeans, dconf, dtable, dW, db, s); break;
-    case 8: o16 ? launch_prim_t<8, 16>(sc, g, dmeans, dconf, dtable, dW, db, s) : launch_prim_t<8, 8>(sc, g, dmeans, dconf, dtable, dW, db, s); break;
+    case 1: o16 ? launch_prim_t<1, 16>(sc, g, dmeans, dconf, dtable, dW, s) : launch_prim_t<1, 8>(sc, g, dmeans, dconf, dtable, dW, s); break;
+    case 2: o16 ? launch_prim_t<2, 16>(sc, g, dmeans, dconf, dtable, dW, s) : launch_prim_t<2, 8>(sc, g, dmeans, dconf, dtable, dW, s); break;
+    case 4: o16 ? launch_prim_t<4, 16>(sc, g, dmeans, dconf, dtable, dW, s) : launch_prim_t<4, 8>(sc, g, dmeans, dconf, dtable, dW, s); break;
+    case 8: o16 ? launch_prim_t<8, 16>(sc, g, dmeans, dconf, dtable, dW, s) : launch_prim_t<8, 8>(sc, g, dmeans, dconf, dtable, dW, s); break;
     default: break;
   }
   stage_end(kStBwdPrim, s);
