@@ -52,7 +52,10 @@ struct Carver {
 
 int props_stride(int O) { return O > 8 ? 16 : 8; }
 
+// Mapped pinned host words the forward reads the overlap count from (this
+// thread's; the device address is the same under unified addressing).
 thread_local uint64_t* g_pinned = nullptr;
+thread_local uint32_t* g_pinned_dev = nullptr;
 thread_local cudaEvent_t g_events[64] = {};
 
 cudaEvent_t event_for_device() {
@@ -360,10 +363,16 @@ int forward_impl(
   launch_offsets_scan(sc, g, sorted_idx, s);
   stage_end(kStOffsets, s);
   if (!g_pinned) {
-    cudaError_t e = cudaHostAlloc((void**)&g_pinned, 64, cudaHostAllocPortable);
+    cudaError_t e = cudaHostAlloc((void**)&g_pinned, 64, cudaHostAllocPortable | cudaHostAllocMapped);
     if (e != cudaSuccess) return cuda_fail(e, "pinned staging buffer");
+    e = cudaHostGetDevicePointer((void**)&g_pinned_dev, g_pinned, 0);
+    if (e != cudaSuccess) {
+      cudaFreeHost(g_pinned);
+      g_pinned = nullptr;
+      return cuda_fail(e, "pinned staging buffer address");
+    }
   }
-  cudaMemcpyAsync(g_pinned, g.status, 16, cudaMemcpyDeviceToHost, s);
+  launch_publish_status(g.status, g_pinned_dev, s);
   cudaEvent_t ev = event_for_device();
   cudaEventRecord(ev, s);
   // The feature stage depends only on preprocess: queue it before blocking on
@@ -374,8 +383,9 @@ int forward_impl(
   if ((rc = check(s, debug, "features", g.status))) return rc;
   cudaError_t e = cudaEventSynchronize(ev);
   if (e != cudaSuccess) return cuda_fail(e, "overlap count readback");
-  const uint32_t st0 = (uint32_t)(g_pinned[0] & 0xffffffffu);
-  const uint64_t R = g_pinned[1];
+  const volatile uint64_t* pinned = g_pinned;
+  const uint32_t st0 = (uint32_t)(pinned[0] & 0xffffffffu);
+  const uint64_t R = pinned[1];
   if (st0) return fail(VI_ERR_DEVICE, "device status 0x%x after binning", st0);
   if (R >= (1ull << 30)) return fail(VI_ERR_TOO_MANY_OVERLAPS, "%llu overlaps exceed 2^30", (unsigned long long)R);
 

@@ -178,6 +178,15 @@ __global__ void __launch_bounds__(256) ranges_kernel(uint64_t R, const uint32_t*
   if (i == R - 1) ranges[2 * cur + 1] = (uint32_t)R;
 }
 
+// Copies status words 0..3 (the status bits and the overlap count) into mapped
+// pinned host memory.  A kernel rather than a device-to-host copy, so that the
+// host's read of the count does not queue behind large device-to-host copies a
+// caller runs on other streams in the same copy engine.
+__global__ void publish_status_kernel(const uint32_t* __restrict__ status, volatile uint32_t* host_dst) {
+  if (threadIdx.x < 4) host_dst[threadIdx.x] = status[threadIdx.x];
+  __threadfence_system();
+}
+
 __global__ void __launch_bounds__(256) mark_visible_kernel(int P, const float* __restrict__ means,
                                                            const float* __restrict__ view, bool* __restrict__ present) {
   int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -212,6 +221,11 @@ void launch_ranges(uint64_t R, const uint32_t* sorted_tiles, uint32_t* ranges, s
   cudaMemsetAsync(ranges, 0, tiles * 2 * sizeof(uint32_t), s);
   if (R == 0) return;
   ranges_kernel<<<(unsigned)((R + 255) / 256), 256, 0, s>>>(R, sorted_tiles, ranges);
+  note_launches(1);
+}
+
+void launch_publish_status(const uint32_t* status, uint32_t* host_mapped, cudaStream_t s) {
+  publish_status_kernel<<<1, 32, 0, s>>>(status, host_mapped);
   note_launches(1);
 }
 

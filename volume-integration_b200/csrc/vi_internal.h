@@ -149,6 +149,8 @@ void launch_duplicate(const Scene& sc, const GeomState& g, const uint32_t* sorte
                       cudaStream_t s);
 void launch_ranges(uint64_t R, const uint32_t* sorted_tiles, uint32_t* ranges, size_t tiles, cudaStream_t s);
 void launch_mark_visible(int P, const float* means, const float* view, bool* present, cudaStream_t s);
+// Status words 0..3 into mapped pinned host memory (host_mapped: its device address).
+void launch_publish_status(const uint32_t* status, uint32_t* host_mapped, cudaStream_t s);
 void launch_features(const Scene& sc, GeomState& g, cudaStream_t s);
 void launch_render(const Scene& sc, const GeomState& g, const uint32_t* point_list, ImgState& im,
                    float* out_color, float* out_feat, float* vis, cudaStream_t s);
