@@ -260,6 +260,29 @@ int check(cudaStream_t s, int debug, const char* where, const uint32_t* status) 
 
 }  // namespace
 
+cudaError_t begin_status_read(const uint32_t* status, cudaStream_t s) {
+  if (!g_pinned) {
+    cudaError_t e = cudaHostAlloc((void**)&g_pinned, 64, cudaHostAllocPortable | cudaHostAllocMapped);
+    if (e != cudaSuccess) return e;
+    e = cudaHostGetDevicePointer((void**)&g_pinned_dev, g_pinned, 0);
+    if (e != cudaSuccess) {
+      cudaFreeHost(g_pinned);
+      g_pinned = nullptr;
+      return e;
+    }
+  }
+  launch_publish_status(status, g_pinned_dev, s);
+  return cudaEventRecord(event_for_device(), s);
+}
+
+cudaError_t finish_status_read(uint32_t words[4]) {
+  const cudaError_t e = cudaEventSynchronize(event_for_device());
+  if (e != cudaSuccess) return e;
+  const volatile uint32_t* pinned = reinterpret_cast<const volatile uint32_t*>(g_pinned);
+  for (int i = 0; i < 4; i++) words[i] = pinned[i];
+  return cudaSuccess;
+}
+
 // Records a message for vi_last_error() and returns code (for other translation units).
 int set_error(int code, const char* msg) { return fail(code, "%s", msg); }
 
@@ -362,30 +385,19 @@ int forward_impl(
   stage_begin(kStOffsets, s);
   launch_offsets_scan(sc, g, sorted_idx, s);
   stage_end(kStOffsets, s);
-  if (!g_pinned) {
-    cudaError_t e = cudaHostAlloc((void**)&g_pinned, 64, cudaHostAllocPortable | cudaHostAllocMapped);
-    if (e != cudaSuccess) return cuda_fail(e, "pinned staging buffer");
-    e = cudaHostGetDevicePointer((void**)&g_pinned_dev, g_pinned, 0);
-    if (e != cudaSuccess) {
-      cudaFreeHost(g_pinned);
-      g_pinned = nullptr;
-      return cuda_fail(e, "pinned staging buffer address");
-    }
-  }
-  launch_publish_status(g.status, g_pinned_dev, s);
-  cudaEvent_t ev = event_for_device();
-  cudaEventRecord(ev, s);
+  cudaError_t e = begin_status_read(g.status, s);
+  if (e != cudaSuccess) return cuda_fail(e, "overlap count readback");
   // The feature stage depends only on preprocess: queue it before blocking on
   // the overlap count so the GPU works while the host waits.
   stage_begin(kStFeatures, s);
   launch_features(sc, g, s);
   stage_end(kStFeatures, s);
   if ((rc = check(s, debug, "features", g.status))) return rc;
-  cudaError_t e = cudaEventSynchronize(ev);
+  uint32_t words[4];
+  e = finish_status_read(words);
   if (e != cudaSuccess) return cuda_fail(e, "overlap count readback");
-  const volatile uint64_t* pinned = g_pinned;
-  const uint32_t st0 = (uint32_t)(pinned[0] & 0xffffffffu);
-  const uint64_t R = pinned[1];
+  const uint32_t st0 = words[0];
+  const uint64_t R = (uint64_t)words[2] | ((uint64_t)words[3] << 32);
   if (st0) return fail(VI_ERR_DEVICE, "device status 0x%x after binning", st0);
   if (R >= (1ull << 30)) return fail(VI_ERR_TOO_MANY_OVERLAPS, "%llu overlaps exceed 2^30", (unsigned long long)R);
 

@@ -713,8 +713,8 @@ extern "C" int vi_bin_gaussians(int P, int image_width, int image_height, const 
     sorted_idx = alt ? gb.g.didx_alt : gb.g.didx;
     launch_offsets_scan(sc, gb.g, sorted_idx, s);
     uint32_t st[4] = {0, 0, 0, 0};
-    cudaError_t e = cudaMemcpyAsync(st, gb.g.status, sizeof st, cudaMemcpyDeviceToHost, s);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    cudaError_t e = begin_status_read(gb.g.status, s);
+    if (e == cudaSuccess) e = finish_status_read(st);
     if (e != cudaSuccess) return set_error(VI_ERR_CUDA, cudaGetErrorString(e));
     if (st[0]) return gfail(VI_ERR_DEVICE, "vi_bin_gaussians: device status 0x%llx", st[0]);
     total = (uint64_t)st[2] | ((uint64_t)st[3] << 32);

@@ -21,6 +21,14 @@ int set_error(int code, const char* msg);
 // Bits of a tile id for `tiles` tiles (the reference's getHigherMsb).
 int tile_bits(size_t tiles);
 
+// Reads status words 0..3 back to the host without a device-to-host copy (a
+// tiny copy would queue behind a caller's large read-backs in the copy engine):
+// begin_status_read queues a one-warp kernel on `s` that writes them into this
+// thread's mapped pinned buffer, finish_status_read waits for it and returns
+// them.  One read in flight per host thread.
+cudaError_t begin_status_read(const uint32_t* status, cudaStream_t s);
+cudaError_t finish_status_read(uint32_t words[4]);
+
 // Blocks of `threads` threads and `smem` dynamic shared bytes that the current
 // device holds resident at once (SM count x blocks per SM), for persistent
 // grids that loop over their work.
