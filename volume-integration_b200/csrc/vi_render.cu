@@ -19,6 +19,10 @@ namespace vi {
 namespace {
 
 constexpr int kBatch = 64;
+// Entries whose record keys a warp loads at once during a batch's set-up: all
+// of its kBatch / 8 entries (loading them in two or four rounds, with fewer
+// registers, measured slower).
+constexpr int kKeyGroup = kBatch / (VI_TILE_PIX / 32);
 
 template <int OMAX>
 __global__ void __launch_bounds__(VI_TILE_PIX) render_kernel(Scene sc, const uint32_t* __restrict__ point_list,
@@ -37,7 +41,6 @@ __global__ void __launch_bounds__(VI_TILE_PIX) render_kernel(Scene sc, const uin
   __shared__ unsigned long long mask[VI_TILE_PIX];
   __shared__ uint8_t slot[VI_TILE_PIX * kBatch];
   __shared__ uint32_t ent_rec[kBatch];
-  __shared__ uint32_t ent_len[kBatch];
   __shared__ uint32_t ent_flag[kBatch];  // kBwdDiffers of the entry's primitive
   __shared__ float ent_depth[kBatch];
 
@@ -89,34 +92,55 @@ __global__ void __launch_bounds__(VI_TILE_PIX) render_kernel(Scene sc, const uin
   for (uint32_t base = r0; base < r1; base += kBatch) {
     if (__syncthreads_count(!done) == 0) break;
     const int nb = (int)min((uint32_t)kBatch, r1 - base);
-    if (tid < nb) {
-      const uint32_t q = point_list[base + tid];
-      const uint32_t rc = rec_cnt[q], n = rc & ~kBwdDiffers;
-      ent_flag[tid] = rc & kBwdDiffers;
-      const uint32_t* keys = rec_key + (size_t)q * V;
-      uint32_t lo = 0, hi = n;  // first record with key >= klo
-      while (lo < hi) {
-        uint32_t mid = (lo + hi) >> 1;
-        if (keys[mid] < klo) lo = mid + 1; else hi = mid;
-      }
-      uint32_t e = lo;
-      while (e < n && keys[e] < klo + 256u) e++;
-      ent_rec[tid] = (uint32_t)((size_t)q * V + lo);
-      ent_len[tid] = e - lo;
-      ent_depth[tid] = depths[q];
-    }
     mask[tid] = 0ull;
     __syncthreads();
-    // Warp w scatters the records of entries w, w+8, ...
+    // Warp w takes entries w, w+8, ...: lane i fetches entry w+8i's primitive,
+    // record count and depth; then every lane loads one record key of each of
+    // those primitives at once (lane = record slot, V <= 27), and one ballot per
+    // entry finds the records in this tile (contiguous: records are grouped by
+    // tile).  Two rounds of loads per batch, where a search per entry chains
+    // several.
     {
       const int w = tid >> 5, lane = tid & 31;
-      for (int e = w; e < nb; e += VI_TILE_PIX / 32) {
-        const uint32_t len = ent_len[e];
-        if ((uint32_t)lane < len) {
-          const uint32_t lp = rec_key[ent_rec[e] + lane] & 255u;
-          slot[lp * kBatch + e] = (uint8_t)lane;
+      constexpr int kPer = kBatch / (VI_TILE_PIX / 32);  // entries per warp
+      const int el = w + (VI_TILE_PIX / 32) * lane;
+      uint32_t q_l = 0u, rc_l = 0u;
+      float d_l = 0.0f;
+      if (lane < kPer && el < nb) {
+        q_l = point_list[base + el];
+        rc_l = rec_cnt[q_l];
+        d_l = depths[q_l];
+      }
+#pragma unroll
+      for (int i0 = 0; i0 < kPer; i0 += kKeyGroup) {
+      uint32_t key[kKeyGroup];
+#pragma unroll
+      for (int j = 0; j < kKeyGroup; j++) {
+        const int i = i0 + j, e = w + (VI_TILE_PIX / 32) * i;
+        const uint32_t q = __shfl_sync(0xffffffffu, q_l, i);
+        const uint32_t n = __shfl_sync(0xffffffffu, rc_l, i) & ~kBwdDiffers;
+        key[j] = (e < nb && (uint32_t)lane < n) ? rec_key[(size_t)q * V + lane] : 0xffffffffu;
+      }
+#pragma unroll
+      for (int j = 0; j < kKeyGroup; j++) {
+        const int i = i0 + j, e = w + (VI_TILE_PIX / 32) * i;
+        if (e >= nb) break;  // warp-uniform
+        const uint32_t in = __ballot_sync(0xffffffffu, (key[j] & ~255u) == klo);
+        const uint32_t q = __shfl_sync(0xffffffffu, q_l, i);
+        const uint32_t rc = __shfl_sync(0xffffffffu, rc_l, i);
+        const float d = __shfl_sync(0xffffffffu, d_l, i);
+        const uint32_t lo = in ? (uint32_t)__ffs(in) - 1u : 0u;
+        if (lane == 0) {
+          ent_rec[e] = (uint32_t)((size_t)q * V + lo);
+          ent_flag[e] = rc & kBwdDiffers;
+          ent_depth[e] = d;
+        }
+        if ((in >> lane) & 1u) {
+          const uint32_t lp = key[j] & 255u;
+          slot[lp * kBatch + e] = (uint8_t)(lane - lo);
           atomicOr(&mask[lp], 1ull << e);
         }
+      }
       }
     }
     __syncthreads();
