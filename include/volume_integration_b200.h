@@ -50,7 +50,11 @@ const char* vi_last_error(void);
  * callbacks and must be passed unchanged to the backward.  Inputs follow the
  * reference's positional order; resolution/do_hash hold hashgrid_levels
  * entries, primes 3, viewmatrix/projmatrix 16 column-major floats, bg_color 3.
- * Blocks the host once, to read the overlap count.
+ * Blocks the host once, to read the overlap count.  That count reaches the
+ * host through 64 bytes of mapped pinned host memory (allocated on the calling
+ * thread's first forward and kept), written by a one-warp kernel, so the wait
+ * does not queue behind device-to-host copies the caller runs on other
+ * streams.
  */
 int vi_integrate_primitives(
     vi_resize_fn geom_buffer, void* geom_user, vi_resize_fn binning_buffer, void* binning_user,
