@@ -32,6 +32,20 @@ typedef enum vi_status {
   VI_ERR_DEVICE = 6            /* a kernel latched an error in the state's status word */
 } vi_status;
 
+/*
+ * Bits of the device status word that kernels latch instead of trapping (a
+ * bounded wait that gives up, an impossible count).  A call that reads a set bit
+ * returns VI_ERR_DEVICE, and vi_last_error() names the bits.  Who reads it:
+ *   - vi_integrate_primitives(_ex): always after preprocess, depth sort and the
+ *     overlap scan (with the overlap count); after every later stage (tile sort,
+ *     render) only when debug is set, or afterwards through vi_read_device_status;
+ *   - vi_integrate_primitives_backward(_ex): only when debug is set;
+ *   - vi_sort_pairs, vi_sort_pairs_noalloc: always (they wait for the sort).
+ * After VI_DEVICE_LOOKBACK_TIMEOUT the sorted output of that call is unspecified.
+ */
+#define VI_DEVICE_LOOKBACK_TIMEOUT 0x1u /* a sort's look-back gave up after its spin limit */
+#define VI_DEVICE_RECORD_OVERFLOW 0x2u  /* more records than grid points for a primitive */
+
 /* Grows the caller's byte buffer to at least nbytes and returns its device
  * address (reference: resizeFunctional, integrate_primitives.cu:54-68). */
 typedef char* (*vi_resize_fn)(void* user, size_t nbytes);
@@ -148,7 +162,11 @@ int vi_mark_visible(int P, const float* means3D, const float* viewmatrix, const 
  * cub::DeviceRadixSort::SortPairs (reference:
  * cuda_integrator/integrator_impl.cu:341-349).  temp must hold
  * vi_sort_pairs_temp_bytes(n, begin_bit, end_bit) bytes; keys_in/vals_in are
- * used as scratch and are clobbered.  n < 2^30.
+ * used as scratch and are clobbered.  n < 2^30.  The kernels run on `stream`;
+ * the call then blocks the host until they finish, to read the sort's status
+ * word (its first 4 bytes sit 0-255 bytes into temp, at the first 256-byte
+ * boundary) and returns VI_ERR_DEVICE if a look-back wait gave up
+ * (VI_DEVICE_LOOKBACK_TIMEOUT).
  */
 size_t vi_sort_pairs_temp_bytes(uint64_t n, int begin_bit, int end_bit);
 int vi_sort_pairs(uint64_t* keys_in, uint32_t* vals_in, uint64_t* keys_out, uint32_t* vals_out, uint64_t n,
@@ -159,19 +177,40 @@ int vi_sort_pairs(uint64_t* keys_in, uint32_t* vals_in, uint64_t* keys_out, uint
  * every byte of device memory, or that cannot take the implicit device-wide
  * synchronisation of cudaMalloc/cudaFree mid-frame).  No counterpart in the
  * reference.  Same contract as vi_sort_pairs except that the sort's scratch lives
- * in a fixed 3 MiB device array inside libvi_b200.so (held by every GPU that loads
- * the library until the process exits), so no temp buffer is passed:
+ * in a fixed device array of VI_SORT_NOALLOC_SCRATCH_BYTES inside libvi_b200.so
+ * (held by every GPU that loads the library until the process exits), so no temp
+ * buffer is passed:
  *   - n <= VI_SORT_NOALLOC_MAX_KEYS; larger n returns VI_ERR_INVALID_ARGUMENT;
  *   - keys_in/vals_in are clobbered; the sorted pairs land in keys_out/vals_out;
  *   - the first call on a device looks up the array's device address (make that
- *     first call before any stream capture);
+ *     first call before any stream capture) and keeps it for the process: do not
+ *     call it on a device after cudaDeviceReset() there;
  *   - every call uses the same array: calls that overlap on the GPU (other
- *     streams, other threads) race and must be serialised by the caller.
+ *     streams, other threads) race and must be serialised by the caller;
+ *   - like vi_sort_pairs it blocks the host until the sort ends and returns
+ *     VI_ERR_DEVICE after a look-back timeout (VI_DEVICE_LOOKBACK_TIMEOUT); the
+ *     status word is read with a 4-byte device-to-host copy into host stack
+ *     memory.
  * Calls no cudaMalloc, cudaFree or allocating library routine.
  */
 #define VI_SORT_NOALLOC_MAX_KEYS (1u << 20)
+#define VI_SORT_NOALLOC_SCRATCH_BYTES (3u << 20)
 int vi_sort_pairs_noalloc(uint64_t* keys_in, uint32_t* vals_in, uint64_t* keys_out, uint32_t* vals_out, uint64_t n,
                           int begin_bit, int end_bit, void* stream);
+
+/*
+ * Testing hook for the sort's bounded look-back wait; no counterpart in the
+ * reference.  vi_sort_pairs with tile 0 of every digit pass withheld: one CTA
+ * fewer runs and the tile counter starts at 1, so tile 1 waits for a predecessor
+ * that never publishes and gives up after spin_limit polls (1 <= spin_limit <=
+ * 2^20; vi_sort_pairs uses 2^20).  Every launched CTA still works on a tile that
+ * exists and writes only inside keys_out/vals_out.  n must span at least two
+ * tiles of 3072 keys.  Returns VI_ERR_DEVICE with *device_status (host) holding
+ * VI_DEVICE_LOOKBACK_TIMEOUT; the outputs are then unspecified.
+ */
+int vi_sort_pairs_withheld_tile(uint64_t* keys_in, uint32_t* vals_in, uint64_t* keys_out, uint32_t* vals_out,
+                                uint64_t n, int begin_bit, int end_bit, void* temp, size_t temp_bytes,
+                                int spin_limit, uint32_t* device_status, void* stream);
 
 /* Number of key bits the reference sorts on: 32 + getHigherMsb(tiles)
  * (reference: cuda_integrator/integrator_impl.cu:47-62, :341). */

@@ -39,6 +39,21 @@ def test_c_abi_host_checks_without_gpu():
     assert rc == 1 and b"layout" in lib.vi_last_error()
 
 
+def test_noalloc_sort_scratch_holds_its_largest_sort():
+    # VI_SORT_NOALLOC_MAX_KEYS keys over all 64 bits must fit the fixed scratch
+    # array; vi_sort_pairs_temp_bytes covers the same carving plus 512 bytes of
+    # alignment and status word, so it bounds the no-allocation sort's need.
+    text = open(HEADER).read()
+    max_keys = eval(re.search(r"#define VI_SORT_NOALLOC_MAX_KEYS \((.*?)\)", text).group(1).replace("u", ""))
+    scratch = eval(re.search(r"#define VI_SORT_NOALLOC_SCRATCH_BYTES \((.*?)\)", text).group(1).replace("u", ""))
+    lib = ctypes.CDLL(LIB)
+    lib.vi_sort_pairs_temp_bytes.restype = ctypes.c_size_t
+    lib.vi_sort_pairs_temp_bytes.argtypes = [ctypes.c_uint64, ctypes.c_int, ctypes.c_int]
+    assert max_keys == 1 << 20 and scratch == 3 << 20
+    for begin, end in ((0, 64), (0, 32), (7, 64)):
+        assert lib.vi_sort_pairs_temp_bytes(max_keys, begin, end) <= scratch
+
+
 def test_settings_fields_and_defaults_match_reference():
     import volume_integration as vi
     s = vi.IntegrationSettings()

@@ -286,6 +286,21 @@ cudaError_t finish_status_read(uint32_t words[4]) {
 // Records a message for vi_last_error() and returns code (for other translation units).
 int set_error(int code, const char* msg) { return fail(code, "%s", msg); }
 
+static_assert(VI_ERR_LOOKBACK_TIMEOUT == VI_DEVICE_LOOKBACK_TIMEOUT, "status bits of the public header");
+static_assert(VI_ERR_RECORD_OVERFLOW == VI_DEVICE_RECORD_OVERFLOW, "status bits of the public header");
+
+int read_sort_status(const uint32_t* status, uint32_t* out, cudaStream_t s, const char* where) {
+  uint32_t st = 0;  // host stack memory: no allocation on this path
+  cudaError_t e = cudaMemcpyAsync(&st, status, sizeof st, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e, where);
+  if (out) *out = st;
+  if (st)
+    return fail(VI_ERR_DEVICE, "%s: device status 0x%x%s", where, st,
+                (st & VI_ERR_LOOKBACK_TIMEOUT) ? " (a look-back wait gave up; the output is unspecified)" : "");
+  return VI_OK;
+}
+
 int tile_bits(size_t tiles) {
   // getHigherMsb (integrator_impl.cu:47-62)
   uint32_t n = (uint32_t)tiles, msb = sizeof(n) * 4, step = msb;
@@ -587,9 +602,11 @@ extern "C" size_t vi_sort_pairs_temp_bytes(uint64_t n, int begin_bit, int end_bi
   return sort_temp_bytes(n, 8, begin_bit, end_bit) + 512;
 }
 
-extern "C" int vi_sort_pairs(uint64_t* keys_in, uint32_t* vals_in, uint64_t* keys_out, uint32_t* vals_out, uint64_t n,
-                             int begin_bit, int end_bit, void* temp, size_t temp_bytes, void* stream) {
-  cudaStream_t s = (cudaStream_t)stream;
+// Shared body of vi_sort_pairs and its withheld-tile testing hook.
+static int sort_pairs_impl(uint64_t* keys_in, uint32_t* vals_in, uint64_t* keys_out, uint32_t* vals_out, uint64_t n,
+                           int begin_bit, int end_bit, void* temp, size_t temp_bytes, int spin_limit, bool withheld,
+                           uint32_t* device_status, cudaStream_t s) {
+  if (device_status) *device_status = 0;
   if (n >= (1ull << 30)) return fail(VI_ERR_INVALID_ARGUMENT, "n=%llu must be < 2^30", (unsigned long long)n);
   if (begin_bit < 0 || end_bit > 64 || begin_bit > end_bit) return fail(VI_ERR_INVALID_ARGUMENT, "bit range [%d,%d)", begin_bit, end_bit);
   if (temp_bytes < vi_sort_pairs_temp_bytes(n, begin_bit, end_bit)) return fail(VI_ERR_INVALID_ARGUMENT, "temp too small");
@@ -598,13 +615,33 @@ extern "C" int vi_sort_pairs(uint64_t* keys_in, uint32_t* vals_in, uint64_t* key
   uint32_t* status = (uint32_t*)t;  // first 256 bytes
   SortTemp st;
   sort_temp_carve(t + 256, n, 8, begin_bit, end_bit, st);
+  if (withheld && st.tiles < 2)
+    return fail(VI_ERR_INVALID_ARGUMENT, "withheld-tile sort needs at least two tiles (n=%llu)", (unsigned long long)n);
   cudaMemsetAsync(status, 0, 4, s);
-  bool alt = onesweep_sort_u64(keys_in, vals_in, keys_out, vals_out, n, begin_bit, end_bit, st, status, s);
+  const bool alt = withheld ? onesweep_sort_u64_withheld(keys_in, vals_in, keys_out, vals_out, n, begin_bit, end_bit, st,
+                                                         status, spin_limit, s)
+                            : onesweep_sort_u64(keys_in, vals_in, keys_out, vals_out, n, begin_bit, end_bit, st, status, s);
   if (!alt) {
     cudaMemcpyAsync(keys_out, keys_in, n * 8, cudaMemcpyDeviceToDevice, s);
     cudaMemcpyAsync(vals_out, vals_in, n * 4, cudaMemcpyDeviceToDevice, s);
   }
-  return check(s, 0, "sort_pairs", nullptr);
+  int rc = check(s, 0, "sort_pairs", nullptr);
+  if (rc) return rc;
+  return read_sort_status(status, device_status, s, "sort_pairs");
+}
+
+extern "C" int vi_sort_pairs(uint64_t* keys_in, uint32_t* vals_in, uint64_t* keys_out, uint32_t* vals_out, uint64_t n,
+                             int begin_bit, int end_bit, void* temp, size_t temp_bytes, void* stream) {
+  return sort_pairs_impl(keys_in, vals_in, keys_out, vals_out, n, begin_bit, end_bit, temp, temp_bytes, 1 << 20, false,
+                         nullptr, (cudaStream_t)stream);
+}
+
+extern "C" int vi_sort_pairs_withheld_tile(uint64_t* keys_in, uint32_t* vals_in, uint64_t* keys_out, uint32_t* vals_out,
+                                           uint64_t n, int begin_bit, int end_bit, void* temp, size_t temp_bytes,
+                                           int spin_limit, uint32_t* device_status, void* stream) {
+  if (spin_limit < 1 || spin_limit > (1 << 20)) return fail(VI_ERR_INVALID_ARGUMENT, "spin_limit=%d outside [1, 2^20]", spin_limit);
+  return sort_pairs_impl(keys_in, vals_in, keys_out, vals_out, n, begin_bit, end_bit, temp, temp_bytes, spin_limit, true,
+                         device_status, (cudaStream_t)stream);
 }
 
 extern "C" int vi_get_state_layout(int P, int64_t num_rendered, int image_height, int image_width,

@@ -18,6 +18,11 @@ void note_launches(int n);
 // Records a message for vi_last_error() and returns code.
 int set_error(int code, const char* msg);
 
+// Waits for `s`, copies the 4-byte sort status word to the host (stack memory,
+// no allocation) and returns VI_ERR_DEVICE with a message when a bit is set;
+// *out (may be null) receives the word.
+int read_sort_status(const uint32_t* status, uint32_t* out, cudaStream_t s, const char* where);
+
 // Bits of a tile id for `tiles` tiles (the reference's getHigherMsb).
 int tile_bits(size_t tiles);
 
@@ -58,6 +63,11 @@ bool onesweep_sort_u32(uint32_t* keys, uint32_t* vals, uint32_t* alt_keys, uint3
                        int begin_bit, int end_bit, const SortTemp& t, uint32_t* status, cudaStream_t s);
 bool onesweep_sort_u64(uint64_t* keys, uint32_t* vals, uint64_t* alt_keys, uint32_t* alt_vals, uint64_t n,
                        int begin_bit, int end_bit, const SortTemp& t, uint32_t* status, cudaStream_t s);
+// The same sort with tile 0 of every pass withheld and look-back waits limited
+// to spin_limit polls (testing the bounded wait; needs t.tiles >= 2).
+bool onesweep_sort_u64_withheld(uint64_t* keys, uint32_t* vals, uint64_t* alt_keys, uint32_t* alt_vals, uint64_t n,
+                                int begin_bit, int end_bit, const SortTemp& t, uint32_t* status, int spin_limit,
+                                cudaStream_t s);
 
 // ---------------------------------------------------------------------------
 // Geometry state: everything sized by the primitive count P.

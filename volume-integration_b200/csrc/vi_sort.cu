@@ -7,9 +7,10 @@
 // (cuda_integrator/integrator_impl.cu:341-349).  Stability gives the same
 // permutation as CUB on the same bit range.
 //
-// Look-back waits are bounded: after kSpinLimit polls a CTA latches
-// VI_ERR_LOOKBACK_TIMEOUT in the status word, stops waiting and writes only
-// in-bounds positions, so a lost predecessor can never hang the GPU.
+// Look-back waits are bounded: after a spin limit (kSpinLimit polls in
+// production) a CTA latches VI_ERR_LOOKBACK_TIMEOUT in the status word, stops
+// waiting and writes only in-bounds positions, so a lost predecessor can never
+// hang the GPU.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -43,6 +44,15 @@ __device__ __forceinline__ void st_volatile(uint32_t* p, uint32_t v) { *(volatil
 template <typename K>
 __device__ __forceinline__ uint32_t digit_of(K k, int shift, uint32_t mask) {
   return (uint32_t)(k >> shift) & mask;
+}
+
+__global__ void fill_u32_kernel(uint32_t* p, uint32_t v, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) p[i] = v;
+}
+void fill_u32_async(uint32_t* p, uint32_t v, int n, cudaStream_t s) {
+  fill_u32_kernel<<<1, 32, 0, s>>>(p, v, n);
+  note_launches(1);
 }
 
 // Digit histograms of every pass in one read of the keys.
@@ -97,7 +107,8 @@ template <typename K>
 __global__ void __launch_bounds__(kSortThreads) onesweep_pass_kernel(
     const K* __restrict__ keys_in, const uint32_t* __restrict__ vals_in, K* __restrict__ keys_out,
     uint32_t* __restrict__ vals_out, uint64_t n, int shift, uint32_t mask, const uint32_t* __restrict__ digit_base,
-    uint32_t* __restrict__ lookback, uint32_t* __restrict__ tile_counter, uint32_t* __restrict__ status) {
+    uint32_t* __restrict__ lookback, uint32_t* __restrict__ tile_counter, uint32_t* __restrict__ status,
+    int spin_limit) {
   constexpr int kItems = SortCfg<K>::kItems;
   constexpr int kTile = kSortThreads * kItems;
   constexpr int kWarps = kSortThreads / 32;
@@ -177,7 +188,7 @@ __global__ void __launch_bounds__(kSortThreads) onesweep_pass_kernel(
     while (pred >= 0) {
       uint32_t v = ld_volatile(lookback + (uint64_t)pred * kRadix + d);
       if ((v & ~kCountMask) == 0) {
-        if (++spins > kSpinLimit) {
+        if (++spins > spin_limit) {
           timed_out = true;
           break;
         }
@@ -218,14 +229,22 @@ __global__ void __launch_bounds__(kSortThreads) onesweep_pass_kernel(
   }
 }
 
+// withhold_first_tile (testing only): the tile counters start at 1 and one CTA
+// fewer is launched, so tile 0 never publishes and tile 1's look-back runs into
+// its spin limit.  Every launched CTA still gets a tile id below t.tiles.
 template <typename K>
 bool sort_impl(K* keys, uint32_t* vals, K* alt_keys, uint32_t* alt_vals, uint64_t n, int begin_bit, int end_bit,
-               const SortTemp& t, uint32_t* status, cudaStream_t s) {
+               const SortTemp& t, uint32_t* status, cudaStream_t s, int spin_limit = kSpinLimit,
+               bool withhold_first_tile = false) {
   if (n <= 1 || end_bit <= begin_bit) return false;
+  if (withhold_first_tile && t.tiles < 2) return false;
   constexpr int kTile = kSortThreads * SortCfg<K>::kItems;
   const int passes = t.passes;
   cudaMemsetAsync(t.hist, 0, sizeof(uint32_t) * kRadix * passes, s);
-  cudaMemsetAsync(t.counters, 0, sizeof(uint32_t) * passes, s);
+  if (withhold_first_tile)
+    fill_u32_async(t.counters, 1u, passes, s);
+  else
+    cudaMemsetAsync(t.counters, 0, sizeof(uint32_t) * passes, s);
   cudaMemsetAsync(t.lookback, 0, sizeof(uint32_t) * kRadix * (size_t)t.tiles * passes, s);
   int hblocks = (int)std::min<uint64_t>((n + 255) / 256, 148 * 8);
   hist_kernel<K><<<hblocks, 256, 0, s>>>(keys, n, begin_bit, end_bit, passes, t.hist);
@@ -238,9 +257,9 @@ bool sort_impl(K* keys, uint32_t* vals, K* alt_keys, uint32_t* alt_vals, uint64_
   for (int p = 0; p < passes; p++) {
     int shift = begin_bit + 8 * p;
     int bits = min(8, end_bit - shift);
-    onesweep_pass_kernel<K><<<t.tiles, kSortThreads, 0, s>>>(
+    onesweep_pass_kernel<K><<<t.tiles - (withhold_first_tile ? 1u : 0u), kSortThreads, 0, s>>>(
         kin, vin, kout, vout, n, shift, (1u << bits) - 1, t.hist + p * kRadix,
-        t.lookback + (size_t)p * t.tiles * kRadix, t.counters + p, status);
+        t.lookback + (size_t)p * t.tiles * kRadix, t.counters + p, status, spin_limit);
     K* tk = kin;
     kin = kout;
     kout = tk;
@@ -281,6 +300,12 @@ bool onesweep_sort_u32(uint32_t* keys, uint32_t* vals, uint32_t* alt_keys, uint3
 bool onesweep_sort_u64(uint64_t* keys, uint32_t* vals, uint64_t* alt_keys, uint32_t* alt_vals, uint64_t n,
                        int begin_bit, int end_bit, const SortTemp& t, uint32_t* status, cudaStream_t s) {
   return sort_impl<uint64_t>(keys, vals, alt_keys, alt_vals, n, begin_bit, end_bit, t, status, s);
+}
+
+bool onesweep_sort_u64_withheld(uint64_t* keys, uint32_t* vals, uint64_t* alt_keys, uint32_t* alt_vals, uint64_t n,
+                                int begin_bit, int end_bit, const SortTemp& t, uint32_t* status, int spin_limit,
+                                cudaStream_t s) {
+  return sort_impl<uint64_t>(keys, vals, alt_keys, alt_vals, n, begin_bit, end_bit, t, status, s, spin_limit, true);
 }
 
 }  // namespace vi

@@ -22,7 +22,7 @@ namespace {
 // Scratch for at most VI_SORT_NOALLOC_MAX_KEYS keys over any bit range: 256 bytes
 // of status word, then the sort's histograms, look-back words and counters.
 // Every GPU that loads the library keeps this array until the process exits.
-constexpr size_t kScratchBytes = 3u << 20;
+constexpr size_t kScratchBytes = VI_SORT_NOALLOC_SCRATCH_BYTES;
 static __device__ __align__(256) unsigned char g_sort_scratch[kScratchBytes];
 
 std::mutex g_mu;
@@ -75,5 +75,7 @@ extern "C" int vi_sort_pairs_noalloc(uint64_t* keys_in, uint32_t* vals_in, uint6
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(VI_ERR_CUDA, cudaGetErrorString(e));
-  return VI_OK;
+  // A look-back wait that gave up leaves positions of keys_out unwritten: wait
+  // for the sort and report it rather than return unsorted output as VI_OK.
+  return read_sort_status(status, nullptr, s, "vi_sort_pairs_noalloc");
 }
