@@ -9,8 +9,8 @@ scaling, views sharded across GPUs) and the gradients are summed over ranks
 with one NCCL all-reduce per step.
 
 Prints one JSON line (rank 0).  `--impl reference` times the CPU restatement
-of the reference algorithm on the host cores instead (there is no reference
-CPU implementation; its CUDA extension is not run).
+of the reference algorithm on the host cores instead: the reference has no CPU
+implementation of the path.
 """
 import argparse
 import json

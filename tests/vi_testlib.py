@@ -88,10 +88,16 @@ def run_gpu(means, conf, s, dcolor=None, dfeat=None, state=True):
 
 
 def raw_forward(means, conf, s):
-    """Positional call of _C.integrate_primitives, exactly as the reference's Python layer makes it."""
+    """Positional call of _C.integrate_primitives, exactly as the reference's Python layer makes it
+    (integrate_primitives_ex with the same arguments when the settings carry the hash_bounds or
+    exact_gradients extensions)."""
+    import volume_integration as vi
     from volume_integration import _C
     G = s.grid_size
-    return _C.integrate_primitives(
+    hb, flags = vi._hash_bounds(s), vi._flags(s)
+    fn = _C.integrate_primitives if hb is None and not flags else \
+        (lambda *a: _C.integrate_primitives_ex(*a, hb or [], flags))
+    return fn(
         means.contiguous().float(), conf.reshape(means.shape[0], G ** 3).contiguous().float(), s.primitive_scale,
         s.viewmatrix, s.projmatrix, s.cam_pos, s.tanfovx, s.tanfovy, s.image_height, s.image_width, s.near_plane,
         s.max_distance, s.feature_table, s.resolution, s.do_hash, s.primes, s.feature_offset, s.linear_weights,
