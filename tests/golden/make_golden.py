@@ -3,10 +3,10 @@ inputs, used to pin the CPU oracle (tests/test_golden.py) and to check the
 CUDA path (tests/test_gpu_golden.py).
 
 Run on a machine with a GPU, from the repository root, after
-`make -C oracle/ref` has built oracle/_ref/libviref_{G,O3}.so from the
-reference sources:
+`make -C oracle/ref REF=<reference checkout>` has built
+oracle/_ref/libviref_{G,O3}.so from the reference sources:
 
-    python tests/golden/make_golden.py [--out DIR] [binning] [full]
+    python tests/golden/make_golden.py [--out DIR] [binning] [full] [<full case name> ...]
 
 Two kinds of fixtures:
 
@@ -233,14 +233,24 @@ def full_case(libs, name, **kw):
     print("full", name, "seed", seed, "R", d["G_num_rendered"], "contrib", d["G_n_contrib"].tolist())
 
 
-def full_fixtures(libs):
-    full_case(libs, "px1")
-    full_case(libs, "px1_k3", K=3)
-    full_case(libs, "px1_genus2", genus=2)
-    full_case(libs, "px1_bg", bg=(0.2, 0.4, 0.6), table_range=0.5)
-    full_case(libs, "px1_ties", ties=True)
-    full_case(libs, "px1_grid2", G=2)
-    full_case(libs, "px2", W=2, P=16)
+FULL_CASES = {
+    "px1": {},
+    "px1_k3": dict(K=3),
+    "px1_genus2": dict(genus=2),
+    "px1_bg": dict(bg=(0.2, 0.4, 0.6), table_range=0.5),
+    "px1_ties": dict(ties=True),
+    "px1_grid2": dict(G=2),
+    "px2": dict(W=2, P=16),
+    # 4^3 and 5^3 grids (the reference's MAX_GRID_SIZE is 5, forward.cu:204-205)
+    "px1_grid4": dict(G=4, P=12),
+    "px1_grid5": dict(G=5, P=8),
+}
+
+
+def full_fixtures(libs, names=None):
+    for name, kw in FULL_CASES.items():
+        if names is None or name in names:
+            full_case(libs, name, **kw)
 
 
 if __name__ == "__main__":
@@ -257,3 +267,6 @@ if __name__ == "__main__":
         binning_fixtures(libs)
     if "full" in which:
         full_fixtures(libs)
+    picked = [a for a in which if a in FULL_CASES]  # single full cases by name
+    if picked:
+        full_fixtures(libs, picked)

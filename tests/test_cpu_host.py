@@ -161,6 +161,18 @@ def _forward_ex_args(flags, bounds):
     return args, cb
 
 
+@pytest.mark.parametrize("G,flags,rc,msg", [(6, 0, 2, b"grid_size=6"), (4, 1, 2, b"exact_gradients needs grid_size"),
+                                            (5, 1, 2, b"exact_gradients needs grid_size")])
+def test_c_abi_grid_size_limits(G, flags, rc, msg):
+    # grid sizes 1..5 are supported (the reference's MAX_GRID_SIZE); the
+    # exact-gradient extension only up to 3
+    lib = _lib()
+    args, _keep = _forward_ex_args(flags, None)
+    args[34] = ctypes.c_int(G)
+    assert lib.vi_integrate_primitives_ex(*args) == rc
+    assert msg in lib.vi_last_error()
+
+
 @pytest.mark.parametrize("flags,bounds,msg", [
     (2, None, b"unknown flags"),
     (0, (0.0, 0.0, 0.0, 1.0, -1.0, 1.0), b"hash_bounds axis 1"),

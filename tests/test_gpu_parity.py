@@ -60,6 +60,17 @@ CUSTOM = {
     "near_camera": dict(dist=1.2, extent=0.8, scale=0.3),
     "dense_overlap": dict(P=2000, scale=0.15, extent=0.7),
     "tiny_table_range": dict(table_range=1e-4),
+    # grids of 4^3 and 5^3 points (the reference's MAX_GRID_SIZE is 5)
+    "grid4": dict(G=4),
+    "grid5": dict(G=5),
+    "grid4_genus2": dict(G=4, genus=2),
+    "grid5_genus2": dict(G=5, genus=2, P=150),
+    "grid5_F4L16_D64": dict(G=5, F=4, L=16),
+    "grid4_fout8_o12": dict(G=4, Fout=8),
+    "grid4_K3": dict(G=4, K=3),
+    "grid5_near_camera": dict(G=5, dist=1.2, extent=0.8, scale=0.3),
+    "grid4_dense_overlap": dict(G=4, P=1500, scale=0.15, extent=0.7),
+    "grid5_T_not_pow2": dict(G=5, T=3001, log2_T=11),
 }
 
 

@@ -153,7 +153,7 @@ GeomState geom_layout(char* base, size_t P, int V, int O, int D) {
   g.differs_list = c.take<uint32_t>(P);
   // Last, so the offsets above do not depend on D.
   g.cls_base = c.take<uint32_t>(P);
-  const size_t want = P * (size_t)V;
+  const size_t want = V <= 32 ? P * (size_t)V : 0;  // grids of G = 4, 5 gather again in the backward
   size_t cap = D > 0 ? std::min(want, phi_cache_max_bytes() / (sizeof(float) * (size_t)D)) : 0;
   cap = std::min(cap, (size_t)kCornerCache - 1);  // the top bit of cls_base marks box-corner primitives
   g.phi_cap = (uint32_t)cap;
@@ -202,8 +202,9 @@ int make_scene(Scene& sc, int P, const float* means3D, const float* conf, float 
     return fail(VI_ERR_UNSUPPORTED, "num_output_channels=%u: only 3 colour channels are implemented (as the "
                                     "reference, forward.cu:838)", channels);
   if (P < 0 || H < 0 || W < 0 || K < 0) return fail(VI_ERR_INVALID_ARGUMENT, "negative size (P=%d H=%d W=%d K=%d)", P, H, W, K);
-  if (G < 1 || G > 3)
-    return fail(VI_ERR_UNSUPPORTED, "grid_size=%d: the kernels map one grid point per lane and need 1 <= G <= 3", G);
+  if (G < 1 || G > 5)
+    return fail(VI_ERR_UNSUPPORTED, "grid_size=%d: supported sizes are 1..5 (the reference's MAX_GRID_SIZE, "
+                                    "forward.cu:204-205)", G);
   if (!(F == 1 || F == 2 || F == 4 || F == 8))
     return fail(VI_ERR_UNSUPPORTED, "input_feature_dim=%u: supported values are 1, 2, 4, 8", F);
   if (L < 1 || L * F > 64) return fail(VI_ERR_UNSUPPORTED, "hashgrid_levels*input_feature_dim=%u must be in [1, 64]", L * F);
@@ -349,6 +350,8 @@ int forward_impl(
   if (rc) return rc;
   if (flags & ~VI_FLAG_EXACT_GRADIENTS) return fail(VI_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
   sc.exact = (flags & VI_FLAG_EXACT_GRADIENTS) != 0;
+  if (sc.exact && sc.V > 32)
+    return fail(VI_ERR_UNSUPPORTED, "exact_gradients needs grid_size <= 3 (got %d)", grid_size);
   if (intermediate_feature_dim != hashgrid_levels * input_feature_dim)
     return fail(VI_ERR_INVALID_ARGUMENT,
                 "intermediate_feature_dim=%u must equal hashgrid_levels*input_feature_dim=%u (the reference reads "
@@ -467,6 +470,8 @@ int backward_impl(
   if (rc) return rc;
   if (flags & ~VI_FLAG_EXACT_GRADIENTS) return fail(VI_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
   sc.exact = (flags & VI_FLAG_EXACT_GRADIENTS) != 0;
+  if (sc.exact && sc.V > 32)
+    return fail(VI_ERR_UNSUPPORTED, "exact_gradients needs grid_size <= 3 (got %d)", grid_size);
   if (feature_table_size < (uint64_t)sc.T * sc.L * sc.F)
     return fail(VI_ERR_INVALID_ARGUMENT, "feature_table_size=%llu < feature_offset*L*F", (unsigned long long)feature_table_size);
   // Zeroed outputs (integrator_impl.cu:573-577).

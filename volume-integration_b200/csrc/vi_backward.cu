@@ -70,12 +70,10 @@ template <int OMAX>
 __device__ __noinline__ void recompute_props(const Scene& sc, uint32_t q, int px, int py, float* props) {
   const int V = sc.V, G = sc.G, D = sc.D, O = sc.O;
   const Stencil st = make_stencil(sc.genus);
-  float conf[32];
-  uint32_t posm = 0;
-  for (int g = 0; g < V; g++) {
-    conf[g] = sc.conf[(size_t)q * V + g];
-    if (conf[g] > 0.0f) posm |= 1u << g;
-  }
+  const float* conf = sc.conf + (size_t)q * V;
+  uint32_t posm[kWideWords] = {0u, 0u, 0u, 0u};
+  for (int g = 0; g < V; g++)
+    if (conf[g] > 0.0f) posm[g >> 5] |= 1u << (g & 31);
   const float3 c = make_float3(sc.means[3 * q], sc.means[3 * q + 1], sc.means[3 * q + 2]);
   float acc[OMAX];
   for (int o = 0; o < OMAX; o++) acc[o] = 0.0f;
@@ -85,7 +83,7 @@ __device__ __noinline__ void recompute_props(const Scene& sc, uint32_t q, int px
     const float3 pos = grid_pos(c, g, G, sc.step, sc.gof);
     const float2 sb = project(pos, sc.proj, sc.W, sc.H, false);
     if (pix_coord(sb.x) != px || pix_coord(sb.y) != py) continue;
-    const float mag = occ_mag(posm, g, G, st);
+    const float mag = occ_mag_w(posm, grid_point(g, G, 0.0f), G, st);
     if (!(mag > 1e-7f)) continue;
     gather_generic(sc, pos, phi);
     const float wgt = fmul(conf[g], mag);
@@ -947,9 +945,184 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
   }
 }
 
+// Per-primitive backward for grids of more than 32 points (G = 4, 5; the
+// reference allows up to 5, backward.cu:26-33): one block of kWideThreads per
+// primitive, thread g = grid point g, following the reference's formula
+// (backward.cu:404-765) record by record.  For every contributing record p, the
+// grid points whose backward screen position lies in p's pixel are the
+// occupancy of g'_{p,.}; each grid point accumulates
+//   v_g = sum_p g'_{p,g} dpre_p, vA_g (the terms with |g' conf_g| > 1e-9) and
+//   E_g = w_g dpre_{p(g)} for the record of its own pixel,
+// then gathers its features phi_g, scatters W^T (conf_g vA_g) into the table
+// gradient at its corners, writes dconf_g = v_g . (W phi_g), and the block sums
+// dW += E_g (x) phi_g (one global atomic per element at the end).
+template <int F, int OMAX, bool POW2>
+__global__ void __launch_bounds__(kWideThreads) backward_prim_wide_kernel(Scene sc, GeomState g,
+                                                                         float* __restrict__ dconf,
+                                                                         float* __restrict__ dtable,
+                                                                         float* __restrict__ dW) {
+  extern __shared__ float4 smem4[];
+  float* smem = reinterpret_cast<float*>(smem4);
+  const int L = sc.L, D = L * F, DP = bwd_dp(D), O = sc.O, V = sc.V, G = sc.G;
+  float* W_s = smem;                                           // [OMAX][DP]
+  float* resf_s = W_s + OMAX * DP;                             // [L]
+  int* res_s = reinterpret_cast<int*>(resf_s + pad4(L));       // [L]
+  int* hash_s = res_s + pad4(L);                               // [L]
+  float* dpre_s = reinterpret_cast<float*>(hash_s + pad4(L));  // [kWideThreads][OMAX] dL/dpre of record j
+  float* el_s = dpre_s + kWideThreads * OMAX;                  // [kWideThreads][OMAX] E of grid point g
+  float* phi_s = el_s + kWideThreads * OMAX;                   // [kWideThreads][DP] phi of grid point g
+  float* dw_s = phi_s + kWideThreads * DP;                     // [OMAX][D] the block's dW
+  uint32_t* rp_s = reinterpret_cast<uint32_t*>(dw_s + OMAX * D);  // [kWideThreads] pixel + 1 of record j
+  uint32_t* ef_s = rp_s + kWideThreads;                        // [kWideThreads] grid point g has E
+  uint32_t* occ_s = ef_s + kWideThreads;                       // [kWideWords] conf > 0
+  uint32_t* inm_s = occ_s + kWideWords;                        // [kWideWords] in the pixel of one record
+  int* misc_s = reinterpret_cast<int*>(inm_s + kWideWords);    // [4] claimed primitive
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+  for (int i = t; i < OMAX * DP; i += blockDim.x) {
+    const int o = i / DP, d = i % DP;
+    W_s[i] = o < O && d < D ? sc.Wl[o * D + d] : 0.0f;
+  }
+  for (int i = t; i < L; i += blockDim.x) {
+    res_s[i] = sc.res[i];
+    resf_s[i] = (float)sc.res[i];
+    hash_s[i] = sc.do_hash[i];
+  }
+  for (int i = t; i < OMAX * D; i += blockDim.x) dw_s[i] = 0.0f;
+  const Stencil st = make_stencil(sc.genus);
+  const bool act = t < V;
+  const GridPt gp = grid_point(act ? t : 0, G, sc.gof);
+  const uint32_t p0 = (uint32_t)__ldg(sc.primes), p1 = (uint32_t)__ldg(sc.primes + 1),
+                 p2 = (uint32_t)__ldg(sc.primes + 2);
+  for (;;) {
+    __syncthreads();  // the previous primitive's shared reads are done
+    if (t == 0) misc_s[0] = (int)atomicAdd(g.status + 5, 1u);
+    __syncthreads();
+    const int q = misc_s[0];
+    if (q >= sc.P) break;
+    if ((g.rec_cnt[q] & ~kBwdDiffers) == 0u) continue;
+    const size_t s0 = (size_t)q * V;
+    const uint32_t rp = act ? g.rec_pix[s0 + t] : 0u;  // record slot t
+    rp_s[t] = rp;
+    if (rp) {
+      const float4* src = reinterpret_cast<const float4*>(g.rec_dpre + (s0 + t) * OMAX);
+      float4* dst = reinterpret_cast<float4*>(dpre_s + t * OMAX);
+#pragma unroll
+      for (int o4 = 0; o4 < OMAX / 4; o4++) dst[o4] = src[o4];
+    }
+    const float conf = act ? sc.conf[s0 + t] : 0.0f;
+    const float3 c = make_float3(sc.means[3 * q], sc.means[3 * q + 1], sc.means[3 * q + 2]);
+    const float3 pos = grid_pos_rel(c, gp.rel, sc.step);
+    const float2 sb = project(pos, sc.proj, sc.W, sc.H, false);  // backward.cu:325
+    const int bx = pix_coord(sb.x), by = pix_coord(sb.y);
+    const int bpix = (act && bx >= 0 && bx < sc.W && by >= 0 && by < sc.H) ? by * sc.W + bx : -1;
+    const uint32_t occw = __ballot_sync(0xffffffffu, act && conf > 0.0f);
+    if (lane == 0) occ_s[w] = occw;
+    if (!__syncthreads_or(rp != 0u)) continue;  // also publishes rp_s, dpre_s, occ_s
+    const float mag = act ? occ_mag_w(occ_s, gp, G, st) : 0.0f;
+    const float wE = (act && conf > 0.0f && mag > 1e-7f) ? fmul(conf, mag) : 0.0f;
+    float v[OMAX], vA[OMAX], e[OMAX];
+#pragma unroll
+    for (int o = 0; o < OMAX; o++) v[o] = vA[o] = e[o] = 0.0f;
+    bool hasE = false, hasV = false, hasA = false;
+    for (int j = 0; j < V; j++) {
+      const uint32_t rj = rp_s[j];
+      if (rj == 0u) continue;  // block-uniform
+      const int ppix = (int)rj - 1;
+      const uint32_t inw = __ballot_sync(0xffffffffu, bpix == ppix);
+      __syncthreads();  // the previous record's inm_s reads are done
+      if (lane == 0) inm_s[w] = inw;
+      __syncthreads();
+      if (bpix == ppix && wE != 0.0f) {
+        hasE = true;
+#pragma unroll
+        for (int o = 0; o < OMAX; o++) e[o] = fmul(wE, dpre_s[j * OMAX + o]);
+      }
+      const float gpv = act ? occ_mag_w(inm_s, gp, G, st) : 0.0f;
+      if (gpv > 1e-7f) {
+        hasV = true;
+        const bool doA = fabsf(fmul(gpv, conf)) > 1e-9f;
+        hasA |= doA;
+#pragma unroll
+        for (int o = 0; o < OMAX; o++) {
+          const float x = gpv * dpre_s[j * OMAX + o];
+          v[o] += x;
+          if (doA) vA[o] += x;
+        }
+      }
+    }
+    if (hasE || hasV) {
+      // features of this grid point and the table-gradient scatter, level by level
+      const float3 n = hash_norm(pos, sc.hlo, sc.hext);
+      float cv[OMAX];
+#pragma unroll
+      for (int o = 0; o < OMAX; o++) cv[o] = hasA ? conf * vA[o] : 0.0f;
+#pragma unroll 1
+      for (int l = 0; l < L; l++) {
+        const LevelCorners lc = level_corners(n, res_s[l], resf_s[l], hash_s[l] != 0, p0, p1, p2, sc.T);
+        float A[F], acc[F];
+#pragma unroll
+        for (int f = 0; f < F; f++) {
+          acc[f] = 0.0f;
+          float sum = 0.0f;
+          if (hasA) {
+#pragma unroll
+            for (int o = 0; o < OMAX; o++) sum += W_s[o * DP + l * F + f] * cv[o];
+          }
+          A[f] = sum;
+        }
+        gather_scatter_level<F, POW2>(lc, sc.table + (size_t)l * F, dtable + (size_t)l * F, (uint32_t)D, sc.T,
+                                      sc.Tmask, hasA, A, acc);
+#pragma unroll
+        for (int f = 0; f < F; f++) phi_s[t * DP + l * F + f] = acc[f];
+      }
+      float dX = 0.0f;
+#pragma unroll
+      for (int o = 0; o < OMAX; o++) {
+        float m = 0.0f;
+        for (int i = 0; i < D; i++) m = __fmaf_rn(W_s[o * DP + i], phi_s[t * DP + i], m);
+        dX += v[o] * m;
+      }
+      dconf[s0 + t] = dX;
+    }
+    ef_s[t] = hasE ? 1u : 0u;
+#pragma unroll
+    for (int o = 0; o < OMAX; o++) el_s[t * OMAX + o] = e[o];
+    __syncthreads();
+    // dW += sum_g E_g (x) phi_g: each (output, input) element is owned by one thread
+    for (int it = t; it < O * D; it += kWideThreads) {
+      const int o = it / D, i = it - (it / D) * D;
+      float sum = 0.0f;
+      for (int u = 0; u < V; u++)
+        if (ef_s[u]) sum += el_s[u * OMAX + o] * phi_s[u * DP + i];
+      dw_s[o * D + i] += sum;
+    }
+  }
+  for (int it = t; it < O * D; it += kWideThreads)
+    if (dw_s[it] != 0.0f) atomicAdd(&dW[it], dw_s[it]);
+}
+
+template <int F, int OMAX>
+void launch_prim_wide(const Scene& sc, GeomState& g, float* dconf, float* dtable, float* dW, cudaStream_t s) {
+  const int D = sc.L * F;
+  const size_t smem = sizeof(float) * (OMAX * bwd_dp(D) + 3 * pad4(sc.L) + 2 * kWideThreads * OMAX +
+                                       kWideThreads * bwd_dp(D) + OMAX * D + 2 * kWideThreads + 2 * kWideWords + 4);
+  auto k = sc.Tmask ? backward_prim_wide_kernel<F, OMAX, true> : backward_prim_wide_kernel<F, OMAX, false>;
+  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaMemsetAsync(g.status + 5, 0, sizeof(uint32_t), s);
+  int blocks = resident_blocks(reinterpret_cast<const void*>(k), kWideThreads, smem);
+  blocks = blocks < sc.P ? blocks : sc.P;
+  if (blocks < 1) blocks = 1;
+  k<<<blocks, kWideThreads, smem, s>>>(sc, g, dconf, dtable, dW);
+  note_launches(1);
+}
+
 template <int F, int OMAX>
 void launch_prim_t(const Scene& sc, GeomState& g, float* dmeans, float* dconf, float* dtable, float* dW,
                    cudaStream_t s) {
+  if (sc.V > 32) {  // G = 4, 5 (reference mode only; the API rejects the exact mode there)
+    launch_prim_wide<F, OMAX>(sc, g, dconf, dtable, dW, s);
+    return;
+  }
   const int D = sc.L * F;
   size_t smem = sizeof(float) * (bwd_head_floats(D, sc.L, OMAX) + kBwdWarps * bwd_warp_floats(D, OMAX));
   auto k = sc.exact ? backward_prim_kernel<F, OMAX, true> : backward_prim_kernel<F, OMAX, false>;

@@ -273,8 +273,183 @@ __global__ void __launch_bounds__(kFeatWarps * 32, 3) features_kernel(Scene sc, 
   }
 }
 
+// Grids of G = 4 or 5 (V = 64 or 125 grid points, up to the reference's
+// MAX_GRID_SIZE of 5, forward.cu:204-205): one block of kWideThreads threads per
+// primitive, thread t = grid point t, with the cross-point steps (occupancy
+// stencil, per-pixel sums in grid-point order, record ranking) through shared
+// memory.  Every grid point that contributes gathers its own features (no
+// position classes and no feature cache: the backward gathers again).  The
+// records are the same as the warp kernel's: one per pixel whose occupancy
+// sum passes 1e-7, grouped by tile, ascending.
+template <int F, int OMAX, bool POW2>
+__global__ void __launch_bounds__(kWideThreads) features_wide_kernel(Scene sc, GeomState g) {
+  extern __shared__ float4 smem4[];
+  float* smem = reinterpret_cast<float*>(smem4);
+  const int L = sc.L, D = L * F, DP = feat_dp(D), O = sc.O, V = sc.V, G = sc.G;
+  float* W_s = smem;                                       // [OMAX][DP]
+  float* b_s = W_s + OMAX * DP;                            // [OMAX]
+  float* resf_s = b_s + OMAX;                              // [L]
+  int* res_s = reinterpret_cast<int*>(resf_s + pad4(L));   // [L]
+  int* hash_s = res_s + pad4(L);                           // [L]
+  float* mlp_s = reinterpret_cast<float*>(hash_s + pad4(L));  // [kWideThreads][OMAX] W phi per grid point
+  float* mag_s = mlp_s + kWideThreads * OMAX;                 // [kWideThreads]
+  float* wgt_s = mag_s + kWideThreads;                        // [kWideThreads] conf * mag
+  uint32_t* key_s = reinterpret_cast<uint32_t*>(wgt_s + kWideThreads);  // [kWideThreads] pixel or ~0
+  uint32_t* rtile_s = key_s + kWideThreads;                   // [kWideThreads] tile of a record or ~0
+  uint32_t* occ_s = rtile_s + kWideThreads;                   // [kWideWords] conf > 0 bits
+  int* misc_s = reinterpret_cast<int*>(occ_s + kWideWords);   // [4] claimed primitive
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+  for (int i = t; i < L; i += blockDim.x) {
+    res_s[i] = sc.res[i];
+    resf_s[i] = (float)sc.res[i];
+    hash_s[i] = sc.do_hash[i];
+  }
+  for (int i = t; i < OMAX * DP; i += blockDim.x) {
+    const int o = i / DP, d = i % DP;
+    W_s[i] = o < O && d < D ? sc.Wl[o * D + d] : 0.0f;
+  }
+  for (int i = t; i < OMAX; i += blockDim.x) b_s[i] = i < O ? sc.bl[i] : 0.0f;
+  const Stencil st = make_stencil(sc.genus);
+  const bool act = t < V;
+  const GridPt gp = grid_point(act ? t : 0, G, sc.gof);
+  const uint32_t p0 = (uint32_t)__ldg(sc.primes), p1 = (uint32_t)__ldg(sc.primes + 1),
+                 p2 = (uint32_t)__ldg(sc.primes + 2);
+  for (;;) {
+    __syncthreads();  // the previous primitive's shared reads are done
+    if (t == 0) misc_s[0] = (int)atomicAdd(g.status + 4, 1u);
+    __syncthreads();
+    const int q = misc_s[0];
+    if (q >= sc.P) break;
+    const int r = g.radii[q];
+    if (r <= 0) {
+      if (t == 0) {
+        g.rec_cnt[q] = 0;
+        g.cls_base[q] = kNoCache;
+      }
+      continue;
+    }
+    const float3 c = make_float3(sc.means[3 * q], sc.means[3 * q + 1], sc.means[3 * q + 2]);
+    const float2 m2 = make_float2(g.means2D[2 * q], g.means2D[2 * q + 1]);
+    const float rf = (float)r;
+    const unsigned x0 = min(sc.gx, (unsigned)max(0, (int)fmul(fsub(m2.x, rf), 0.0625f)));
+    const unsigned y0 = min(sc.gy, (unsigned)max(0, (int)fmul(fsub(m2.y, rf), 0.0625f)));
+    const unsigned x1 = min(sc.gx, (unsigned)max(0, (int)fmul(fsub(fadd(fadd(m2.x, rf), 16.0f), 1.0f), 0.0625f)));
+    const unsigned y1 = min(sc.gy, (unsigned)max(0, (int)fmul(fsub(fadd(fadd(m2.y, rf), 16.0f), 1.0f), 0.0625f)));
+    const float conf = act ? sc.conf[(size_t)q * V + t] : 0.0f;
+    const float3 pos = grid_pos_rel(c, gp.rel, sc.step);
+    const float2 sf = project(pos, sc.proj, sc.W, sc.H, true);
+    const float2 sb = project(pos, sc.proj, sc.W, sc.H, false);
+    const int fx = pix_coord(sf.x), fy = pix_coord(sf.y);
+    const uint32_t occw = __ballot_sync(0xffffffffu, act && conf > 0.0f);
+    if (lane == 0) occ_s[w] = occw;
+    const bool differs =
+        __syncthreads_or(act && (fx != pix_coord(sb.x) || fy != pix_coord(sb.y))) != 0;  // also publishes occ_s
+    const float mag = act ? occ_mag_w(occ_s, gp, G, st) : 0.0f;
+    const bool inside = fx >= 0 && fx < sc.W && fy >= 0 && fy < sc.H;
+    const unsigned tx = (unsigned)fx >> 4, ty = (unsigned)fy >> 4;
+    const bool vpt = act && conf > 0.0f && inside && tx >= x0 && tx < x1 && ty >= y0 && ty < y1;
+    const bool need = vpt && mag > 1e-7f;
+    if (need) {
+      // hashgrid features of this grid point (hashgrid.h:244-287), then W phi
+      const float3 n = hash_norm(pos, sc.hlo, sc.hext);
+      float phi[64];
+#pragma unroll 1
+      for (int l = 0; l < L; l++) {
+        float acc[F];
+#pragma unroll
+        for (int f = 0; f < F; f++) acc[f] = 0.0f;
+        const LevelCorners lc = level_corners(n, res_s[l], resf_s[l], hash_s[l] != 0, p0, p1, p2, sc.T);
+        gather_level<F, POW2>(lc, sc.table + (size_t)l * F, (uint32_t)D, sc.T, sc.Tmask, acc);
+#pragma unroll
+        for (int f = 0; f < F; f++) phi[l * F + f] = acc[f];
+      }
+      for (int o = 0; o < OMAX; o++) {
+        float a = 0.0f;
+        for (int i = 0; i < D; i++) a = __fmaf_rn(W_s[o * DP + i], phi[i], a);
+        mlp_s[t * OMAX + o] = a;
+      }
+    }
+    mag_s[t] = mag;
+    wgt_s[t] = need ? fmul(conf, mag) : 0.0f;
+    key_s[t] = vpt ? (uint32_t)fy * (uint32_t)sc.W + (uint32_t)fx : 0xffffffffu;
+    __syncthreads();
+    // The lowest grid point of each pixel sums that pixel's grid points in
+    // grid-point order (forward.cu:481-627) and decides whether it is a record.
+    bool is_rec = false;
+    float props[OMAX];
+    const uint32_t key = key_s[t];
+    if (vpt) {
+      bool lowest = true;
+      for (int u = 0; u < t && lowest; u++) lowest = key_s[u] != key;
+      if (lowest) {
+        float ogs = 0.0f, acc[OMAX];
+#pragma unroll
+        for (int o = 0; o < OMAX; o++) acc[o] = 0.0f;
+        for (int u = t; u < V; u++) {
+          if (key_s[u] != key) continue;
+          const float mg = mag_s[u];
+          ogs = fadd(ogs, mg);
+          if (mg > 1e-7f) {
+            const float wg = wgt_s[u];
+#pragma unroll
+            for (int o = 0; o < OMAX; o++) acc[o] = fadd(acc[o], fmul(mlp_s[u * OMAX + o], wg));
+          }
+        }
+        if (!(ogs < 1e-7f)) {
+          is_rec = true;
+#pragma unroll
+          for (int o = 0; o < OMAX; o++) {
+            const float pre = fadd(acc[o], b_s[o]);
+            props[o] = o < O - 1 ? sigmoidf_(pre) : (o == O - 1 ? expf(pre) : 0.0f);
+          }
+        }
+      }
+    }
+    const uint32_t tkey = ty * sc.gx + tx;
+    rtile_s[t] = is_rec ? tkey : 0xffffffffu;
+    const int nrec = __syncthreads_count(is_rec);
+    if (is_rec) {
+      // grouped by tile, ascending; grid-point order inside a tile
+      uint32_t rank = 0;
+      for (int u = 0; u < V; u++) {
+        const uint32_t tu = rtile_s[u];
+        rank += (tu < tkey || (tu == tkey && u < t)) ? 1u : 0u;
+      }
+      const size_t slot = (size_t)q * V + rank;
+      g.rec_key[slot] = (tkey << 8) | (((unsigned)fy & 15u) << 4) | ((unsigned)fx & 15u);
+      float4* dst = reinterpret_cast<float4*>(g.rec_props + slot * OMAX);
+#pragma unroll
+      for (int o4 = 0; o4 < OMAX / 4; o4++)
+        dst[o4] = make_float4(props[4 * o4], props[4 * o4 + 1], props[4 * o4 + 2], props[4 * o4 + 3]);
+    }
+    if (t == 0) {
+      g.rec_cnt[q] = (uint32_t)nrec | (differs ? kBwdDiffers : 0u);
+      g.cls_base[q] = kNoCache;
+      if (differs && nrec) g.differs_list[atomicAdd(g.status + 7, 1u)] = (uint32_t)q;
+    }
+  }
+}
+
+template <int F, int OMAX, bool POW2>
+void launch_features_wide(const Scene& sc, GeomState& g, cudaStream_t s) {
+  const int D = sc.L * F;
+  const size_t smem = sizeof(float) * (OMAX * feat_dp(D) + OMAX + 3 * pad4(sc.L) + kWideThreads * OMAX +
+                                       4 * kWideThreads + kWideWords + 4);
+  auto k = features_wide_kernel<F, OMAX, POW2>;
+  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  int blocks = resident_blocks(reinterpret_cast<const void*>(k), kWideThreads, smem);
+  blocks = blocks < sc.P ? blocks : sc.P;
+  if (blocks < 1) blocks = 1;
+  k<<<blocks, kWideThreads, smem, s>>>(sc, g);
+  note_launches(1);
+}
+
 template <int F, int OMAX, bool POW2>
 void launch_features_p(const Scene& sc, GeomState& g, cudaStream_t s) {
+  if (sc.V > 32) {
+    launch_features_wide<F, OMAX, POW2>(sc, g, s);
+    return;
+  }
   const int D = sc.L * F;
   size_t smem = sizeof(float) * (feat_head_floats(D, sc.L, OMAX) + kFeatWarps * feat_warp_floats(D, OMAX));
   auto k = features_kernel<F, OMAX, POW2>;

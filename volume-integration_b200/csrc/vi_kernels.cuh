@@ -72,6 +72,31 @@ __device__ __forceinline__ float occ_mag(uint32_t occ, int g, int G, const Stenc
   return occ_mag(occ, grid_point(g, G, 0.0f), G, st);
 }
 
+// occ_mag for grids of more than 32 points (G = 4, 5): the occupancy is a bit
+// array of 32-bit words (bit g of word g / 32).  Same taps, same order of
+// additions as the reference loop (forward.cu:557-611, backward.cu:654-689).
+__device__ __forceinline__ bool occ_bit(const uint32_t* occ, int i) { return (occ[i >> 5] >> (i & 31)) & 1u; }
+__device__ __forceinline__ float occ_mag_w(const uint32_t* occ, const GridPt& p, int G, const Stencil& st) {
+  const int x = p.x, y = p.y, z = p.z;
+  const int off = (st.S - 1) / 2;
+  float gx = 0.0f, gy = 0.0f, gz = 0.0f;
+  for (int s = 0; s < st.S; s++) {
+    int r = s - off, n;
+    n = x + r;
+    if (n >= 0 && n < G && occ_bit(occ, z * G * G + y * G + n)) gx = fadd(gx, st.c[s]);
+    n = y + r;
+    if (n >= 0 && n < G && occ_bit(occ, z * G * G + n * G + x)) gy = fadd(gy, st.c[s]);
+    n = z + r;
+    if (n >= 0 && n < G && occ_bit(occ, n * G * G + y * G + x)) gz = fadd(gz, st.c[s]);
+  }
+  return fadd(fadd(fabsf(gx), fabsf(gy)), fabsf(gz));
+}
+
+// Grids of more than 32 points are handled by block-per-primitive kernels
+// (one thread per grid point, kWideThreads >= 125 = 5^3).
+constexpr int kWideThreads = 128;
+constexpr int kWideWords = kWideThreads / 32;
+
 // F contiguous table floats of one (entry, level).
 template <int F>
 struct FVec {

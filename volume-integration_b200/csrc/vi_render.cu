@@ -24,7 +24,9 @@ constexpr int kBatch = 64;
 // registers, measured slower).
 constexpr int kKeyGroup = kBatch / (VI_TILE_PIX / 32);
 
-template <int OMAX>
+// WIDE: primitives of more than 32 grid points (G = 4, 5), whose records a
+// warp reads 32 slots at a time.
+template <int OMAX, bool WIDE>
 __global__ void __launch_bounds__(VI_TILE_PIX) render_kernel(Scene sc, const uint32_t* __restrict__ point_list,
                                                             const uint32_t* __restrict__ ranges,
                                                             const float* __restrict__ depths,
@@ -99,7 +101,7 @@ __global__ void __launch_bounds__(VI_TILE_PIX) render_kernel(Scene sc, const uin
     // those primitives at once (lane = record slot, V <= 27), and one ballot per
     // entry finds the records in this tile (contiguous: records are grouped by
     // tile).  Two rounds of loads per batch, where a search per entry chains
-    // several.
+    // several.  Grids of more than 32 points take one entry at a time.
     {
       const int w = tid >> 5, lane = tid & 31;
       constexpr int kPer = kBatch / (VI_TILE_PIX / 32);  // entries per warp
@@ -111,6 +113,36 @@ __global__ void __launch_bounds__(VI_TILE_PIX) render_kernel(Scene sc, const uin
         rc_l = rec_cnt[q_l];
         d_l = depths[q_l];
       }
+      if constexpr (WIDE) {
+        // Entry by entry, the primitive's record keys 32 slots at a time; the
+        // records of this tile are contiguous from slot lo.
+        for (int i = 0; i < kPer; i++) {
+          const int e = w + (VI_TILE_PIX / 32) * i;
+          if (e >= nb) break;  // warp-uniform
+          const uint32_t q = __shfl_sync(0xffffffffu, q_l, i);
+          const uint32_t rc = __shfl_sync(0xffffffffu, rc_l, i);
+          const float d = __shfl_sync(0xffffffffu, d_l, i);
+          const uint32_t n = rc & ~kBwdDiffers;
+          int lo = -1;
+          for (uint32_t s0 = 0; s0 < n; s0 += 32) {
+            const uint32_t sl = s0 + (uint32_t)lane;
+            const uint32_t key = sl < n ? rec_key[(size_t)q * V + sl] : 0xffffffffu;
+            const uint32_t in = __ballot_sync(0xffffffffu, (key & ~255u) == klo);
+            if (!in) continue;
+            if (lo < 0) lo = (int)(s0 + (uint32_t)__ffs(in) - 1u);
+            if ((in >> lane) & 1u) {
+              const uint32_t lp = key & 255u;
+              slot[lp * kBatch + e] = (uint8_t)(sl - (uint32_t)lo);
+              atomicOr(&mask[lp], 1ull << e);
+            }
+          }
+          if (lane == 0) {
+            ent_rec[e] = (uint32_t)((size_t)q * V + (lo < 0 ? 0u : (uint32_t)lo));
+            ent_flag[e] = rc & kBwdDiffers;
+            ent_depth[e] = d;
+          }
+        }
+      } else {
 #pragma unroll
       for (int i0 = 0; i0 < kPer; i0 += kKeyGroup) {
       uint32_t key[kKeyGroup];
@@ -140,6 +172,7 @@ __global__ void __launch_bounds__(VI_TILE_PIX) render_kernel(Scene sc, const uin
           slot[lp * kBatch + e] = (uint8_t)(lane - lo);
           atomicOr(&mask[lp], 1ull << e);
         }
+      }
       }
       }
     }
@@ -195,14 +228,11 @@ void launch_render(const Scene& sc, const GeomState& g, const uint32_t* point_li
   const unsigned tiles = sc.gx * sc.gy;
   if (tiles == 0) return;
   note_launches(1);
-  if (sc.O > 8)
-    render_kernel<16><<<tiles, VI_TILE_PIX, 0, s>>>(sc, point_list, im.ranges, g.depths, g.rec_cnt, g.rec_key,
-                                                    g.rec_props, out_color, out_feat, vis, im.final_T, im.n_contrib,
-                                                    im.contrib_idx, im.delta_t, im.contrib_rec, im.trans, im.trig);
-  else
-    render_kernel<8><<<tiles, VI_TILE_PIX, 0, s>>>(sc, point_list, im.ranges, g.depths, g.rec_cnt, g.rec_key,
-                                                   g.rec_props, out_color, out_feat, vis, im.final_T, im.n_contrib,
-                                                   im.contrib_idx, im.delta_t, im.contrib_rec, im.trans, im.trig);
+  auto k = sc.O > 8 ? (sc.V > 32 ? render_kernel<16, true> : render_kernel<16, false>)
+                    : (sc.V > 32 ? render_kernel<8, true> : render_kernel<8, false>);
+  k<<<tiles, VI_TILE_PIX, 0, s>>>(sc, point_list, im.ranges, g.depths, g.rec_cnt, g.rec_key, g.rec_props, out_color,
+                                  out_feat, vis, im.final_T, im.n_contrib, im.contrib_idx, im.delta_t, im.contrib_rec,
+                                  im.trans, im.trig);
 }
 
 }  // namespace vi
