@@ -599,10 +599,24 @@ def cpu_scene(config):
     return _CPU_SCENES[config]
 
 
-def cpu_frame_sample(config, budget_s, threads):
+def cpu_model():
+    """The host CPU's model name (from /proc/cpuinfo), or the platform string."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.lower().startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or platform.machine()
+
+
+def cpu_frame_sample(config, budget_s, threads, timing=None):
     """Times the oracle on a bounded sample of one frame: the full preprocess and
     binning, then render + backward on every k-th tile, extrapolated to all
-    tiles.  Returns (frames/s, description)."""
+    tiles.  Returns (frames/s, description); `timing` (a dict) receives the
+    wall seconds actually spent and the fraction of the frame rendered."""
     _oracle_path()
     import oracle as orc
     sc, dc, dfe = cpu_scene(config)
@@ -632,18 +646,33 @@ def cpu_frame_sample(config, budget_s, threads):
     t_smp = time.perf_counter() - t0
     n = int(mask.sum())
     frame_s = t_bin + t_smp * tiles / n
+    if timing is not None:
+        timing.update(wall_s=t_bin + t_cal + t_smp, sampled_tiles=n, tiles=tiles, frame_s=frame_s)
     desc = (f"{config}: full preprocess + binning ({t_bin:.2f} s), render+backward on every {k}-th tile "
             f"({n}/{tiles} tiles, {t_smp:.2f} s) extrapolated to the frame; {threads} threads")
     return 1.0 / frame_s, desc
 
 
+def cpu_host():
+    return {"cpu_model": cpu_model(), "os_cpu_count": os.cpu_count(), "torch_threads": torch.get_num_threads()}
+
+
 def cpu_baseline(config, budget_s):
     threads = os.cpu_count() or 1
     v, desc = cpu_frame_sample(config, budget_s, threads)
-    return {"value": round(v, 5), "unit": "frames/s", "cores": threads, "kind": "port", "sample": desc}
+    out = {"value": round(v, 5), "unit": "frames/s", "cores": threads, "kind": "port", "sample": desc}
+    out.update(cpu_host())
+    return out
 
 
 def run_reference(args):
+    """The reference algorithm on the host cores (the reference has no CPU
+    implementation of the path; the scalar C restatement of its kernels runs on
+    every core).  A step is one bounded sample of the frame: the full
+    preprocess and binning plus render + backward on every k-th tile, so
+    `ms_per_step` x `steps` is the wall time that actually ran, and `value` is
+    the frame rate extrapolated from each step's sample (frame-equivalent time
+    in `frame_ms`).  Under torchrun rank 0 alone runs (one CPU process)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
@@ -651,19 +680,24 @@ def run_reference(args):
     budget = max(2.0, min(10.0, 150.0 / max(1, args.steps + args.warmup)))
     for _ in range(args.warmup):
         cpu_frame_sample(args.config, budget, threads)
-    vals, descs = [], []
+    frame_s, wall_s, descs, fracs = [], [], [], []
     for _ in range(args.steps):
-        v, d = cpu_frame_sample(args.config, budget, threads)
-        vals.append(v)
+        tm = {}
+        _, d = cpu_frame_sample(args.config, budget, threads, timing=tm)
+        frame_s.append(tm["frame_s"])
+        wall_s.append(tm["wall_s"])
+        fracs.append(tm["sampled_tiles"] / tm["tiles"])
         descs.append(d)
-    value = len(vals) / sum(1.0 / v for v in vals)
+    value = len(frame_s) / sum(frame_s)
     line = {"metric": METRIC, "value": round(value, 5), "unit": "frames/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000.0 / value, 2),
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000.0 * sum(wall_s) / len(wall_s), 1),
+            "frame_ms": round(1000.0 / value, 1), "frame_fraction_per_step": round(sum(fracs) / len(fracs), 5),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "impl": "reference",
-            "config": {"workload": f"{args.config} (same scene and camera as the GPU arm)"},
-            "cpu_baseline": {"value": round(value, 5), "unit": "frames/s", "cores": threads, "kind": "port",
-                             "sample": descs[-1]},
+            "config": {"workload": f"{args.config} (same scene and camera as the GPU arm)",
+                       "processes": "one CPU process on rank 0 at every GPU count"},
+            "cpu_baseline": dict({"value": round(value, 5), "unit": "frames/s", "cores": threads, "kind": "port",
+                                  "sample": descs[-1]}, **cpu_host()),
             "e2e": {"value": round(value, 5), "unit": "frames/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)

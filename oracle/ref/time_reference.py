@@ -26,7 +26,7 @@ import time
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
-for p in (HERE, os.path.join(ROOT, "volume-integration_b200"), os.path.join(ROOT, "tests")):
+for p in (HERE, os.path.join(ROOT, "volume-integration_b200"), os.path.join(ROOT, "oracle"), os.path.join(ROOT, "tests")):
     if p not in sys.path:
         sys.path.insert(0, p)
 
