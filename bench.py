@@ -50,12 +50,17 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=20.0, help="budget of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-ref-cuda", action="store_true",
+                    help="reference arm: skip the timing of the reference's CUDA kernels on the GPU")
     ap.add_argument("--no-aabb", action="store_true", help="skip the run with the hashgrid box at the scene bounds")
     ap.add_argument("--no-gaussians", action="store_true", help="skip the Gaussian front end (extension) measurement")
     ap.add_argument("--gaussians-only", action="store_true",
                     help="measure only the Gaussian front end (extension) and print its object (profiling)")
     ap.add_argument("--exact-gradients", action="store_true",
                     help="exact-gradient backward (extension) instead of the reference's formula")
+    ap.add_argument("--box", default="reference", choices=["reference", "scene"],
+                    help="hashgrid box of the main measurement: the reference's fixed [-1.3, 1.3]^3, or the "
+                         "scene's own bounds (the hash_bounds extension)")
     ap.add_argument("--views", default="one", choices=["one", "all"],
                     help="one: one view per GPU (weak scaling); all: every camera of the scene per step, "
                          "sharded over the GPUs (strong scaling)")
@@ -82,15 +87,20 @@ def settings_from(kw, cam, device, **extra):
 
 def frame_stats(means, conf, s):
     """Overlaps R, visible primitives and pixel contributions of one forward (state views of the C ABI)."""
+    import volume_integration as vi
     from volume_integration import _C
     G = s.grid_size
-    R, _, _, _, geom, binning, img = _C.integrate_primitives(
-        means.contiguous().float(), conf.reshape(means.shape[0], G ** 3).contiguous().float(), s.primitive_scale,
-        s.viewmatrix, s.projmatrix, s.cam_pos, s.tanfovx, s.tanfovy, s.image_height, s.image_width, s.near_plane,
-        s.max_distance, s.feature_table, s.resolution, s.do_hash, s.primes, s.feature_offset, s.linear_weights,
-        s.linear_bias, s.stencil_genus, s.grid_size, s.max_primitives_per_ray, s.occupancy_threshold, s.bg_color,
-        s.input_feature_dim, s.output_feature_dim, s.intermediate_feature_dim, s.hashgrid_levels,
-        s.num_output_channels, s.debug)
+    args = (means.contiguous().float(), conf.reshape(means.shape[0], G ** 3).contiguous().float(), s.primitive_scale,
+            s.viewmatrix, s.projmatrix, s.cam_pos, s.tanfovx, s.tanfovy, s.image_height, s.image_width, s.near_plane,
+            s.max_distance, s.feature_table, s.resolution, s.do_hash, s.primes, s.feature_offset, s.linear_weights,
+            s.linear_bias, s.stencil_genus, s.grid_size, s.max_primitives_per_ray, s.occupancy_threshold, s.bg_color,
+            s.input_feature_dim, s.output_feature_dim, s.intermediate_feature_dim, s.hashgrid_levels,
+            s.num_output_channels, s.debug)
+    hb, flags = vi._hash_bounds(s), vi._flags(s)
+    if hb is None and not flags:
+        R, _, _, _, geom, binning, img = _C.integrate_primitives(*args)
+    else:
+        R, _, _, _, geom, binning, img = _C.integrate_primitives_ex(*args, hb or [], flags)
     v = _C.state_views(geom, binning, img, means.shape[0], R, s.image_height, s.image_width,
                        s.max_primitives_per_ray, G, s.output_feature_dim)
     return {"R": int(R), "Pv": int((v["radii"] > 0).sum()), "Kt": int(v["n_contrib"].sum())}
@@ -121,6 +131,30 @@ def workload(config, rank, world, device, all_views=False):
         df = torch.randn(s.output_feature_dim, s.image_height, s.image_width, generator=gen).to(device)
         views.append((s, dc, df))
     return means.to(device), conf.to(device), views, total
+
+
+STAGE_GROUPS = {"features": ["features"], "render": ["render"], "backward": ["bwd_pixel", "bwd_prim"],
+                "sort": ["depth_sort", "offsets", "binning"], "preprocess": ["preprocess"]}
+
+
+def roofline_of(stage_ms, steps, vstats, views, P, traffic_key):
+    """Roofline object of the dominant stage group: algorithmic bytes per launch
+    (fixed formulas at this run's R, P_v and K_t) over its live average
+    duration (CUDA events on the launching stream), against the measured HBM
+    copy bandwidth; DRAM traffic per launch from the committed ncu capture of
+    this workload when there is one."""
+    peak, peak_kind = measured_peaks()
+    nv = max(1, len(views))
+    abv = [algorithmic_bytes(st, sv, P) for st, (sv, _, _) in zip(vstats, views)]
+    ab = {k: sum(a[k] for a in abv) / nv for k in abv[0]}
+    gms = {g: sum(stage_ms[k] for k in ks) for g, ks in STAGE_GROUPS.items()}
+    dom = max(gms, key=gms.get)
+    per_launch_ms = gms[dom] / max(1, steps * nv)
+    achieved = ab[dom] / (per_launch_ms / 1000.0) / 1e9
+    traffic, traffic_src = measured_traffic(traffic_key, dom)
+    return {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "traffic": traffic, "traffic_source": traffic_src,
+            "peak_kind": peak_kind, "algorithmic_bytes": int(ab[dom]), "ms_per_launch": round(per_launch_ms, 4)}
 
 
 def measured_traffic(config, group):
@@ -250,6 +284,8 @@ def run_ours(args):
         return
 
     means, conf, views, total_views = workload(args.config, rank, world, device, args.views == "all")
+    if args.box == "scene":
+        views = scene_box_views(means, views)
     if args.exact_gradients:
         import dataclasses
         views = [(dataclasses.replace(sv, exact_gradients=True), gc, gf) for sv, gc, gf in views]
@@ -315,22 +351,10 @@ def run_ours(args):
     nv = max(1, len(views))
 
     # roofline of the dominant stage, timed live on the launching stream
-    peak, peak_kind = measured_peaks()
-    abv = [algorithmic_bytes(st, sv, P) for st, (sv, _, _) in zip(vstats, views)]
-    ab = {k: sum(a[k] for a in abv) / nv for k in abv[0]} if abv else algorithmic_bytes(stats, s, P)
     stage_ms = {k: v[0] for k, v in prof.items()}
-    stage_calls = {k: v[1] for k, v in prof.items()}
-    groups = {"features": ["features"], "render": ["render"], "backward": ["bwd_pixel", "bwd_prim"],
-              "sort": ["depth_sort", "offsets", "binning"], "preprocess": ["preprocess"]}
-    gms = {g: sum(stage_ms[k] for k in ks) for g, ks in groups.items()}
-    dom = max(gms, key=gms.get)
-    per_launch_ms = gms[dom] / max(1, args.steps * nv)
-    achieved = ab[dom] / (per_launch_ms / 1000.0) / 1e9
-    traffic, traffic_src = measured_traffic(args.config, dom)
-    roofline = {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(achieved / peak, 4), "traffic": traffic, "traffic_source": traffic_src,
-                "peak_kind": peak_kind, "algorithmic_bytes": int(ab[dom]), "ms_per_launch": round(per_launch_ms, 4)}
-    sort_ms = gms["sort"] / max(1, args.steps)
+    roofline = roofline_of(stage_ms, args.steps, vstats, views, P,
+                           args.config + ("_scenebox" if args.box == "scene" else ""))
+    sort_ms = sum(stage_ms[k] for k in ("depth_sort", "offsets", "binning")) / max(1, args.steps)
     sort_gkeys = stats["R"] / (sort_ms / 1000.0) / 1e9 if sort_ms > 0 else None  # R summed over views
 
     line = {"metric": METRIC, "value": round(value, 3), "unit": "frames/s", "n_gpus": world, "steps": args.steps,
@@ -358,7 +382,7 @@ def run_ours(args):
 
     if not args.no_aabb:
         line["scene_bounds"] = run_scene_bounds(args, step, means, leaves, views, total_views, flush, world, dist,
-                                                device, _C)
+                                                device, _C, vstats, P)
 
     if world == 1 and not args.no_gaussians:
         line["gaussians"] = run_gaussians(args, flush, device)
@@ -375,17 +399,26 @@ def run_ours(args):
         print(json.dumps(line), flush=True)
 
 
-def run_scene_bounds(args, step, means, leaves, views, total_views, flush, world, dist, device, _C):
+def scene_box_views(means, views):
+    """The views with the hashgrid box set to the scene's own bounds (centres'
+    bounding box grown by one primitive edge; the hash_bounds extension)."""
+    import dataclasses
+    pad = float(views[0][0].primitive_scale) if views else 0.0
+    lo = (means.min(0).values - pad).tolist()
+    hi = (means.max(0).values + pad).tolist()
+    return [(dataclasses.replace(sv, hash_bounds=tuple(lo + hi)), gc, gf) for sv, gc, gf in views]
+
+
+def run_scene_bounds(args, step, means, leaves, views, total_views, flush, world, dist, device, _C, vstats, P):
     """The same step with the hashgrid box set to the scene's own bounds (an
     extension field).  The reference's fixed [-1.3, 1.3]^3 box clamps most
     positions of this scene to its faces, where grid points share table
     entries; inside its own bounds every grid point of a primitive reads its own
     cells, which is the harder case for the hashgrid kernels."""
-    import dataclasses
-    pad = float(views[0][0].primitive_scale) if views else 0.0
-    lo = (means.min(0).values - pad).tolist()
-    hi = (means.max(0).values + pad).tolist()
-    vb = [(dataclasses.replace(sv, hash_bounds=tuple(lo + hi)), gc, gf) for sv, gc, gf in views]
+    vb = scene_box_views(means, views)
+    lo, hi = list(vb[0][0].hash_bounds[:3]), list(vb[0][0].hash_bounds[3:])
+    conf = leaves[0].detach()
+    vstats = [frame_stats(means, conf, sv) for sv, _, _ in vb]
     steps = max(1, min(args.steps, 50))
     for _ in range(max(3, args.warmup)):
         step(means, *leaves, vlist=vb)
@@ -408,9 +441,12 @@ def run_scene_bounds(args, step, means, leaves, views, total_views, flush, world
         t = torch.tensor([total_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         total_ms = float(t.item())
-    return {"value": round(total_views * steps / (total_ms / 1000.0), 3), "unit": "frames/s", "steps": steps,
-            "ms_per_step": round(total_ms / steps, 4), "hash_bounds": [round(v, 4) for v in lo + hi],
-            "stage_ms_per_step": {k: round(v[0] / steps, 4) for k, v in prof.items()}}
+    stage_ms = {k: v[0] for k, v in prof.items()}
+    out = {"value": round(total_views * steps / (total_ms / 1000.0), 3), "unit": "frames/s", "steps": steps,
+           "ms_per_step": round(total_ms / steps, 4), "hash_bounds": [round(v, 4) for v in lo + hi],
+           "stage_ms_per_step": {k: round(v / steps, 4) for k, v in stage_ms.items()}}
+    out["roofline"] = roofline_of(stage_ms, steps, vstats, vb, P, args.config + "_scenebox")
+    return out
 
 
 def run_gaussians(args, flush, device):
@@ -657,12 +693,66 @@ def cpu_host():
     return {"cpu_model": cpu_model(), "os_cpu_count": os.cpu_count(), "torch_threads": torch.get_num_threads()}
 
 
+def torch_cpu_sample(config, every=64):
+    """The vectorised PyTorch-CPU restatement (oracle/torch_oracle.py) on the same
+    frame: full preprocess and binning, render + backward on every `every`-th
+    tile, extrapolated to the frame.  Returns a labelled dict."""
+    _oracle_path()
+    import torch_oracle as tor
+    sc0, dc, dfe = cpu_scene(config)
+    t0 = time.perf_counter()
+    sc = tor.Scene(sc0)
+    pre = tor.preprocess(sc)
+    b = tor.binning(sc, pre)
+    t_bin = time.perf_counter() - t0
+    mask = np.zeros(sc0.tiles, np.uint8)
+    mask[::every] = 1
+    t0 = time.perf_counter()
+    f = tor.render(sc, pre, b, tile_mask=mask)
+    tor.backward(sc, pre, b, f, torch.from_numpy(dc), torch.from_numpy(dfe), tile_mask=mask)
+    t_smp = time.perf_counter() - t0
+    n = int(mask.sum())
+    frame_s = t_bin + t_smp * sc0.tiles / n
+    return {"value": round(1.0 / frame_s, 5), "unit": "frames/s", "kind": "port (vectorised PyTorch on CPU)",
+            "threads": torch.get_num_threads(),
+            "sample": f"{config}: full preprocess + binning ({t_bin:.2f} s), render+backward on every {every}-th "
+                      f"tile ({n}/{sc0.tiles} tiles, {t_smp:.2f} s) extrapolated to the frame"}
+
+
 def cpu_baseline(config, budget_s):
     threads = os.cpu_count() or 1
     v, desc = cpu_frame_sample(config, budget_s, threads)
-    out = {"value": round(v, 5), "unit": "frames/s", "cores": threads, "kind": "port", "sample": desc}
+    out = {"value": round(v, 5), "unit": "frames/s", "cores": threads, "kind": "port", "sample": desc,
+           "restatement": "scalar C (oracle/vi_oracle.c), OpenMP over tiles"}
     out.update(cpu_host())
+    try:
+        out["torch_cpu"] = torch_cpu_sample(config)
+    except Exception as e:  # the C port stays the reported value
+        out["torch_cpu"] = {"unavailable": f"{type(e).__name__}: {e}"[:200]}
     return out
+
+
+def ref_cuda_b200(config, reps=2):
+    """The reference's own CUDA kernels on this GPU (oracle/_ref, built from the
+    reference checkout): its binning and backward as shipped, its render in
+    the barrier-fixed form (oracle/ref/barrier_fix.py; the shipped render
+    skips a CTA barrier and reads an unsynchronised shared value, and faulted
+    on a full frame), all at -O3.  Whole Integrator::forward / ::backward calls,
+    CUDA events; the frame rate the north star's >= 5x target is stated
+    against."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle", "ref"))
+    _oracle_path()
+    import reflib
+    import time_reference
+    if not reflib.available("O3_bf"):
+        return {"unavailable": "oracle/_ref/libviref_O3_bf.so not built (make -C oracle/ref REF=...)"}
+    r = time_reference.measure(("O3_bf",), reps=reps, name=config, deadline_s=120.0)
+    o = r["O3_bf"]
+    return {"value": round(o["frames_per_s"], 4), "unit": "frames/s", "build": "-O3, barrier-fixed render",
+            "forward_ms": round(o["forward_ms"], 3), "backward_ms": round(o["backward_ms"], 3),
+            "binning_ms": {k: round(v, 4) for k, v in o["binning_ms"].items()},
+            "cub_sort_gkeys_per_s": round(o["cub_sort_gkeys_per_s"], 3), "num_rendered": o["num_rendered"],
+            "repetitions": o["repetitions"], "workload": r["workload"]}
 
 
 def run_reference(args):
@@ -700,6 +790,11 @@ def run_reference(args):
                                   "sample": descs[-1]}, **cpu_host()),
             "e2e": {"value": round(value, 5), "unit": "frames/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
+    if torch.cuda.is_available() and not args.no_ref_cuda:
+        try:
+            line["ref_cuda_b200"] = ref_cuda_b200(args.config)
+        except Exception as e:
+            line["ref_cuda_b200"] = {"unavailable": f"{type(e).__name__}: {e}"[:200]}
     print(json.dumps(line), flush=True)
 
 

@@ -26,7 +26,7 @@ import time
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
-for p in (HERE, os.path.join(ROOT, "volume-integration_b200"), os.path.join(ROOT, "oracle"), os.path.join(ROOT, "tests")):
+for p in (HERE, os.path.join(ROOT, "volume-integration_b200"), os.path.join(ROOT, "oracle")):
     if p not in sys.path:
         sys.path.insert(0, p)
 
@@ -36,8 +36,15 @@ import reflib  # noqa: E402
 
 
 def headline_inputs(name="headline", view=0):
-    import vi_testlib as tl
-    means, conf, s = tl.scene(name, view=view, device="cuda")
+    """The seeded scene and camera `view` of vi_workloads as CUDA tensors, with the
+    settings as a plain namespace (the reference's IntegrationSettings fields;
+    nothing of this build's library is loaded)."""
+    import types
+    import vi_workloads as wl
+    means, conf, kw, cams = wl.make(name)
+    d = {k: (v.cuda() if torch.is_tensor(v) else v) for k, v in list(kw.items()) + list(cams[view].items())}
+    s = types.SimpleNamespace(**d)
+    means, conf = means.cuda(), conf.cuda()
     gen = torch.Generator().manual_seed(7)
     dc = torch.randn(3, s.image_height, s.image_width, generator=gen).cuda()
     df = torch.randn(s.output_feature_dim, s.image_height, s.image_width, generator=gen).cuda()
