@@ -1133,7 +1133,16 @@ void launch_prim_t(const Scene& sc, GeomState& g, float* dmeans, float* dconf, f
   const int resident = resident_blocks(reinterpret_cast<const void*>(k), kBwdWarps * 32, smem);
   blocks = blocks < resident ? blocks : resident;
   if (blocks < 1) blocks = 1;
-  k<<<blocks, kBwdWarps * 32, smem, s>>>(sc, g, dmeans, dconf, dtable, dW);
+  // the table gradient stays in L2 while primitives scatter into it
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(blocks);
+  cfg.blockDim = dim3(kBwdWarps * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = l2_persist_attr(dtable, (size_t)sc.T * sc.L * F * sizeof(float), attr);
+  cudaLaunchKernelEx(&cfg, k, sc, g, dmeans, dconf, dtable, dW);
   note_launches(1);
 }
 

@@ -459,7 +459,16 @@ void launch_features_p(const Scene& sc, GeomState& g, cudaStream_t s) {
   const int resident = resident_blocks(reinterpret_cast<const void*>(k), kFeatWarps * 32, smem);
   blocks = blocks < resident ? blocks : resident;
   if (blocks < 1) blocks = 1;
-  k<<<blocks, kFeatWarps * 32, smem, s>>>(sc, g);
+  // the table stays in L2 while primitives gather from it
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(blocks);
+  cfg.blockDim = dim3(kFeatWarps * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = l2_persist_attr(sc.table, (size_t)sc.T * sc.L * F * sizeof(float), attr);
+  cudaLaunchKernelEx(&cfg, k, sc, g);
   note_launches(1);
 }
 

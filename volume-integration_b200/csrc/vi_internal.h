@@ -34,6 +34,13 @@ int tile_bits(size_t tiles);
 cudaError_t begin_status_read(const uint32_t* status, cudaStream_t s);
 cudaError_t finish_status_read(uint32_t words[4]);
 
+// Fills *attr with an access-policy window that keeps [base, base + bytes) in
+// L2 (persisting hits, streaming misses) for one kernel launch and returns 1,
+// or returns 0 when it is unavailable or not switched on (VI_L2_WINDOW=1).  The
+// first call on a device sets this process's persisting-L2 carve-out to the
+// device's maximum (a limit of the context, not a setting of the GPU).
+int l2_persist_attr(const void* base, size_t bytes, cudaLaunchAttribute* attr);
+
 // Blocks of `threads` threads and `smem` dynamic shared bytes that the current
 // device holds resident at once (SM count x blocks per SM), for persistent
 // grids that loop over their work.
