@@ -50,6 +50,11 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=20.0, help="budget of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-multiview", action="store_true",
+                    help="skip the 32-view, 3M-primitive scene sharded over the GPUs (strong scaling)")
+    ap.add_argument("--no-other-configs", action="store_true", help="skip the mid and stress scenes (one GPU)")
+    ap.add_argument("--allreduce", default="separate", choices=["separate", "flat"],
+                    help="gradient all-reduce: one per tensor, or one over a flat copy of all of them")
     ap.add_argument("--no-ref-cuda", action="store_true",
                     help="reference arm: skip the timing of the reference's CUDA kernels on the GPU")
     ap.add_argument("--no-aabb", action="store_true", help="skip the run with the hashgrid box at the scene bounds")
@@ -299,7 +304,9 @@ def run_ours(args):
     bl = s.linear_bias.clone().requires_grad_(True)
     leaves = [confp, table, Wl, bl]
 
-    def step(m, c, t, w, b, vlist=views):
+    coalesce = args.allreduce == "flat"
+
+    def step(m, c, t, w, b, vlist=views, reduce=True):
         """Forward + backward of this rank's views, gradients summed over views and ranks."""
         acc = None
         for settings, gc, gf in vlist:
@@ -308,7 +315,8 @@ def run_ours(args):
             acc = list(grads) if acc is None else [a.add_(g) for a, g in zip(acc, grads)]
         if acc is None:  # a rank without views still takes part in the all-reduce
             acc = [torch.zeros_like(x) for x in (c, t, w, b)]
-        allreduce_gradients(acc)  # sum over ranks (no-op with one rank)
+        if reduce:
+            allreduce_gradients(acc, coalesce=coalesce)  # sum over ranks (no-op with one rank)
         return acc
 
     # workload statistics for the roofline (one forward per view, outside timing)
@@ -328,12 +336,15 @@ def run_ours(args):
     launches0 = _C.kernel_launches()
     times = []
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    mid_ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]  # compute done, all-reduce next
     torch.cuda.synchronize()
     clocks.start()
     for i in range(args.steps):
         flush.zero_()
         ev[i][0].record()
-        step(means, *leaves)
+        acc = step(means, *leaves, reduce=False)
+        mid_ev[i].record()
+        allreduce_gradients(acc, coalesce=coalesce)
         ev[i][1].record()
     torch.cuda.synchronize()
     clk = clocks.stop()
@@ -342,10 +353,26 @@ def run_ours(args):
     prof = _C.profile_read(True)
     times = [a.elapsed_time(b) for a, b in ev]
     total_ms = sum(times)
+    breakdown = None
     if world > 1:
         t = torch.tensor([total_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         total_ms = float(t.item())
+        # per step: this rank's compute (forward + backward), and the all-reduce
+        # as seen from the slowest rank (the others also wait for it there)
+        comp = sum(a.elapsed_time(m) for (a, _), m in zip(ev, mid_ev)) / args.steps
+        ar = sum(m.elapsed_time(b) for (_, b), m in zip(ev, mid_ev)) / args.steps
+        cmax = torch.tensor([comp], device=device)
+        cmin = torch.tensor([comp], device=device)
+        dist.all_reduce(cmax, op=dist.ReduceOp.MAX)
+        dist.all_reduce(cmin, op=dist.ReduceOp.MIN)
+        slow = torch.tensor([ar if comp >= float(cmax.item()) - 1e-9 else 1e9], device=device)
+        dist.all_reduce(slow, op=dist.ReduceOp.MIN)
+        breakdown = {"compute_ms_max_rank": round(float(cmax.item()), 4),
+                     "compute_ms_min_rank": round(float(cmin.item()), 4),
+                     "allreduce_ms_slowest_rank": round(float(slow.item()), 4),
+                     "allreduce": "one flat buffer" if coalesce else "one all-reduce per gradient tensor",
+                     "gradient_bytes": int(sum(x.numel() * x.element_size() for x in acc))}
         dist.barrier()
     value = total_views * args.steps / (total_ms / 1000.0)
     nv = max(1, len(views))
@@ -379,6 +406,8 @@ def run_ours(args):
                                         / (total_ms / 1000.0), 1),
             "gpu_launches": int(launches), "gpu_launches_per_step": round(launches / args.steps, 2),
             "clocks": clk}
+    if breakdown:
+        line["step_breakdown"] = breakdown
 
     if not args.no_aabb:
         line["scene_bounds"] = run_scene_bounds(args, step, means, leaves, views, total_views, flush, world, dist,
@@ -389,6 +418,17 @@ def run_ours(args):
 
     if not args.no_e2e:
         line["e2e"] = run_e2e(args, vi, means, conf, views, total_views, world, dist if world > 1 else None, device)
+
+    if world > 1:
+        line["multi_gpu_gradient_check"] = gradient_check(world, rank, device, coalesce)
+    if not args.no_multiview and args.views == "one":
+        del means, conf, views, leaves, confp, table, Wl, bl
+        torch.cuda.empty_cache()
+        line["multiview"] = run_views_all("multiview", args, world, rank, device, dist if world > 1 else None,
+                                          coalesce)
+    if world == 1 and not args.no_other_configs:
+        line["other_configs"] = {c: run_single_view(c, args, flush, device, steps)
+                                 for c, steps in (("mid", 10), ("stress", 3)) if c != args.config}
 
     if world > 1:
         dist.barrier()
@@ -447,6 +487,138 @@ def run_scene_bounds(args, step, means, leaves, views, total_views, flush, world
            "stage_ms_per_step": {k: round(v / steps, 4) for k, v in stage_ms.items()}}
     out["roofline"] = roofline_of(stage_ms, steps, vstats, vb, P, args.config + "_scenebox")
     return out
+
+
+def _leaves(conf, s):
+    return [conf.clone().requires_grad_(True), s.feature_table.clone().requires_grad_(True),
+            s.linear_weights.clone().requires_grad_(True), s.linear_bias.clone().requires_grad_(True)]
+
+
+def run_views_all(config, args, world, rank, device, dist, coalesce):
+    """Every camera of `config` per step, sharded over the ranks (strong
+    scaling; the multiview scene is 32 views of 3M primitives): forward +
+    backward of this rank's views, gradients summed over its views and then
+    over the ranks.  Timed with CUDA events, max over ranks."""
+    import volume_integration as vi
+    from volume_integration.distributed import allreduce_gradients
+    means, conf, views, total = workload(config, rank, world, device, all_views=True)
+    import vi_workloads as wl
+    _, _, kw, cams = wl.make(config) if not views else (None, None, None, None)
+    s0 = views[0][0] if views else settings_from(kw, cams[0], device)
+    leaves = _leaves(conf, s0)
+
+    def one():
+        acc = None
+        for sv, gc, gf in views:
+            oc, of, _ = vi.integrate_primitives(means, *leaves, sv)
+            g = torch.autograd.grad([oc, of], leaves, [gc, gf])
+            acc = list(g) if acc is None else [a.add_(x) for a, x in zip(acc, g)]
+        if acc is None:
+            acc = [torch.zeros_like(x) for x in leaves]
+        allreduce_gradients(acc, coalesce=coalesce)
+    one()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    steps = max(1, min(args.steps, 3))
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        one()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b)
+    if dist is not None:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return {"value": round(total * steps / (ms / 1000.0), 3), "unit": "views/s", "views_per_step": total,
+            "steps": steps, "ms_per_step": round(ms / steps, 3), "n_gpus": world, "scaling": "strong",
+            "workload": f"{config}: {means.shape[0]} primitives, {total} views of "
+                        f"{s0.image_width}x{s0.image_height} sharded over {world} GPU(s), gradients all-reduced "
+                        f"every step"}
+
+
+def run_single_view(config, args, flush, device, steps, warmup=2):
+    """One view of another benchmark scene on this GPU: forward + backward
+    through the autograd Function, L2 flushed between steps, CUDA events."""
+    import volume_integration as vi
+    from volume_integration import _C
+    means, conf, views, _ = workload(config, 0, 1, device)
+    s, gc, gf = views[0]
+    leaves = _leaves(conf, s)
+
+    def one():
+        oc, of, _ = vi.integrate_primitives(means, *leaves, s)
+        torch.autograd.grad([oc, of], leaves, [gc, gf])
+    for _ in range(warmup):
+        one()
+    st = frame_stats(means, conf, s)
+    torch.cuda.synchronize()
+    _C.profile_read(True)
+    _C.profile_enable(True)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for i in range(steps):
+        flush.zero_()
+        ev[i][0].record()
+        one()
+        ev[i][1].record()
+    torch.cuda.synchronize()
+    _C.profile_enable(False)
+    prof = _C.profile_read(True)
+    ms = sum(x.elapsed_time(y) for x, y in ev)
+    stage_ms = {k: v[0] for k, v in prof.items()}
+    tiles = ((s.image_width + 15) // 16) * ((s.image_height + 15) // 16)
+    sort_ms = sum(stage_ms[k] for k in ("depth_sort", "offsets", "binning")) / steps
+    out = {"value": round(steps / (ms / 1000.0), 3), "unit": "frames/s", "steps": steps,
+           "ms_per_step": round(ms / steps, 4),
+           "workload": f"{config}: {means.shape[0]} primitives, {s.image_width}x{s.image_height}, "
+                       f"L={s.hashgrid_levels} F={s.input_feature_dim} T=2^{int(math.log2(s.feature_offset))}, one view",
+           "num_rendered": st["R"], "visible_primitives": st["Pv"], "contributions": st["Kt"], "tiles": tiles,
+           "stage_ms_per_step": {k: round(v / steps, 4) for k, v in stage_ms.items()},
+           "sort_gkeys_per_s": round(st["R"] / (sort_ms / 1000.0) / 1e9, 3) if sort_ms > 0 else None,
+           "roofline": roofline_of(stage_ms, steps, [st], views, means.shape[0], config)}
+    del means, conf, views, leaves
+    torch.cuda.empty_cache()
+    return out
+
+
+def gradient_check(world, rank, device, coalesce):
+    """Multi-GPU gradient parity inside the bench (N >= 2): a small scene with
+    2N cameras, each rank renders its views and the gradients are all-reduced
+    as in the timed step; rank 0 renders every view itself and compares the
+    summed gradients (relative L2 error per tensor, tolerance 1e-3: atomic
+    summation order differs)."""
+    import volume_integration as vi
+    import vi_workloads as wl
+    from volume_integration.distributed import allreduce_gradients, views_for_rank
+    means, conf, kw, _ = wl.make("tiny", table_range=1.0, width=64, height=48, P=1500)
+    c = wl.CONFIGS["tiny"]
+    cams = wl.orbit(2 * world, c["dist"], 64, 48, c["fov"])
+    means, conf = means.to(device), conf.to(device)
+
+    def grads(v):
+        s = settings_from(kw, cams[v], device)
+        gen = torch.Generator().manual_seed(500 + v)
+        dc = torch.randn(3, 48, 64, generator=gen).to(device)
+        df = torch.randn(s.output_feature_dim, 48, 64, generator=gen).to(device)
+        leaves = _leaves(conf, s)
+        oc, of, _ = vi.integrate_primitives(means, *leaves, s)
+        return [g.reshape(-1) for g in torch.autograd.grad([oc, of], leaves, [dc, df])]
+    acc = None
+    for v in views_for_rank(len(cams), rank, world):
+        g = grads(v)
+        acc = g if acc is None else [a + b for a, b in zip(acc, g)]
+    acc = allreduce_gradients([x.contiguous() for x in acc], coalesce=coalesce)
+    if rank != 0:
+        return None
+    ref = None
+    for v in range(len(cams)):
+        g = grads(v)
+        ref = g if ref is None else [a + b for a, b in zip(ref, g)]
+    errs = [float((a - b).norm() / b.norm().clamp_min(1e-30)) for a, b in zip(acc, ref)]
+    return {"views": len(cams), "max_rel_err": max(errs), "tolerance": 1e-3, "ok": max(errs) <= 1e-3,
+            "tensors": ["dL_dconfidences", "dL_dfeature_table", "dL_dlinear_weights", "dL_dlinear_bias"]}
 
 
 def run_gaussians(args, flush, device):

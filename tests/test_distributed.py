@@ -137,3 +137,35 @@ def test_sharded_gradient_sum_nccl(tmp_path):
         seq = g if seq is None else [a + b for a, b in zip(seq, g)]
     tl.assert_grads({k: a.numpy() for k, a in zip(GRAD_KEYS, summed)} | {"dL_dmeans3D": np.zeros(3)},
                     {k: b.cpu().numpy() for k, b in zip(GRAD_KEYS, seq)} | {"dL_dmeans3D": np.zeros(3)})
+
+
+def _coalesce_worker(rank, world, port, out_path):
+    import torch.distributed as dist
+    from datetime import timedelta
+    from volume_integration.distributed import allreduce_gradients
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
+    try:
+        g = torch.Generator().manual_seed(rank)
+        shapes = [(300, 27), (4096,), (8, 32), (8,)]
+        a = [torch.randn(*sh, generator=g) for sh in shapes]
+        b = [x.clone() for x in a]
+        allreduce_gradients(a, coalesce=False)
+        out = allreduce_gradients(b + [None], coalesce=True)
+        assert out[-1] is None
+        if rank == 0:
+            torch.save((a, b), out_path)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_coalesced_allreduce_equals_per_tensor_gloo(tmp_path):
+    # one all-reduce over a flat copy of every gradient sums the same values
+    # as one all-reduce per tensor, and restores each tensor's shape
+    out = str(tmp_path / "coalesced.pt")
+    mp.start_processes(_coalesce_worker, args=(2, _free_port(), out), nprocs=2, join=True, start_method="spawn")
+    a, b = torch.load(out)
+    for x, y in zip(a, b):
+        assert x.shape == y.shape
+        torch.testing.assert_close(x, y, rtol=0, atol=0)

@@ -26,16 +26,36 @@ def views_for_rank(n_views, rank, world):
     return list(range(rank, n_views, world))
 
 
-def allreduce_gradients(grads, group=None):
+_FLAT = {}
+
+
+def allreduce_gradients(grads, group=None, coalesce=False):
     """Sums each gradient tensor over the ranks of `group`, in place, and returns them.
 
     All-reduces are issued asynchronously, largest tensor first (the feature
     table's gradient, then the confidences'), and waited for together, so the
-    collectives queue back to back on the communicator's stream.  `None`
-    entries (parameters without a gradient) are passed through; every rank must
-    pass the same shapes in the same order.  With one rank this is a no-op.
+    collectives queue back to back on the communicator's stream.  With
+    `coalesce` the gradients are instead copied into one flat buffer (kept for
+    the next call of the same size), reduced with a single all-reduce and
+    copied back.  `None` entries (parameters without a gradient) are passed
+    through; every rank must pass the same shapes in the same order.  With one
+    rank this is a no-op.
     """
     if not dist.is_available() or not dist.is_initialized() or dist.get_world_size(group) == 1:
+        return list(grads)
+    live = [g for g in grads if g is not None]
+    if coalesce and len(live) > 1 and len({(g.device, g.dtype) for g in live}) == 1:
+        n = sum(g.numel() for g in live)
+        key = (live[0].device, live[0].dtype, n)
+        flat = _FLAT.get(key)
+        if flat is None:
+            flat = _FLAT.setdefault(key, torch.empty(n, dtype=live[0].dtype, device=live[0].device))
+        torch.cat([g.reshape(-1) for g in live], out=flat)
+        dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group)
+        off = 0
+        for g in live:
+            g.copy_(flat[off:off + g.numel()].view_as(g))
+            off += g.numel()
         return list(grads)
     order = sorted((i for i, g in enumerate(grads) if g is not None), key=lambda i: -grads[i].numel())
     works = []
