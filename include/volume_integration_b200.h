@@ -45,6 +45,7 @@ typedef enum vi_status {
  */
 #define VI_DEVICE_LOOKBACK_TIMEOUT 0x1u /* a sort's look-back gave up after its spin limit */
 #define VI_DEVICE_RECORD_OVERFLOW 0x2u  /* more records than grid points for a primitive */
+#define VI_DEVICE_STAGE_TIMEOUT 0x4u    /* a render tile's bulk-copy wait gave up; it read global memory instead */
 
 /* Grows the caller's byte buffer to at least nbytes and returns its device
  * address (reference: resizeFunctional, integrate_primitives.cu:54-68). */

@@ -261,3 +261,12 @@ def test_feature_cache_fallback(limit, monkeypatch):
     _check(means, conf, s, seed=7)
     means, conf, s = tl.scene("tiny", table_range=1.0)
     _check(means, conf, s, seed=8)
+
+
+@pytest.mark.parametrize("name", ["default", "dense_overlap", "fout8_o12", "K3"])
+def test_render_without_record_staging(name, monkeypatch):
+    # the render's bulk-copy staging of records is the default; the unstaged
+    # form (VI_RENDER_TMA=0, read at every launch) must give the same results
+    monkeypatch.setenv("VI_RENDER_TMA", "0")
+    means, conf, s = tl.custom_scene(seed=zlib.crc32(name.encode()) % 1000, **CUSTOM[name])
+    _check(means, conf, s, seed=3)

@@ -326,6 +326,7 @@ int set_error(int code, const char* msg) { return fail(code, "%s", msg); }
 
 static_assert(VI_ERR_LOOKBACK_TIMEOUT == VI_DEVICE_LOOKBACK_TIMEOUT, "status bits of the public header");
 static_assert(VI_ERR_RECORD_OVERFLOW == VI_DEVICE_RECORD_OVERFLOW, "status bits of the public header");
+static_assert(VI_ERR_STAGE_TIMEOUT == VI_DEVICE_STAGE_TIMEOUT, "status bits of the public header");
 
 int read_sort_status(const uint32_t* status, uint32_t* out, cudaStream_t s, const char* where) {
   uint32_t st = 0;  // host stack memory: no allocation on this path

@@ -19,6 +19,7 @@ namespace vi {
 enum : uint32_t {
   VI_ERR_LOOKBACK_TIMEOUT = 1u << 0,  // a sort look-back gave up after its spin limit
   VI_ERR_RECORD_OVERFLOW = 1u << 1,   // more per-primitive records than grid points (cannot happen)
+  VI_ERR_STAGE_TIMEOUT = 1u << 2,     // a render tile's bulk-copy wait gave up (it fell back to global reads)
 };
 
 struct Mat {

@@ -322,3 +322,45 @@ struct LevelWalk {
 };
 
 }  // namespace vi
+
+// ---- bulk copies global -> shared completed on an mbarrier (sm_90+ PTX) ----
+// Plain cp.async.bulk (no cluster multicast); both addresses 16-byte aligned and
+// the size a multiple of 16, which every caller guarantees.
+namespace vi {
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t* mbar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(mbar)), "r"(count) : "memory");
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* mbar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(mbar)), "r"(bytes)
+               : "memory");
+}
+// Orders this thread's earlier generic-proxy accesses of shared memory before
+// later async-proxy (bulk copy) writes to it.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* mbar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_addr(dst)),
+               "l"(src), "r"(bytes), "r"(smem_addr(mbar))
+               : "memory");
+}
+// Waits for the phase of the given parity to complete, at most `limit` polls
+// (each try_wait suspends for a bounded time).  Returns false on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t* mbar, uint32_t parity, int limit) {
+  for (int i = 0; i < limit; i++) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_addr(mbar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+  }
+  return false;
+}
+}  // namespace vi
