@@ -417,7 +417,9 @@ def run_ours(args):
         line["gaussians"] = run_gaussians(args, flush, device)
 
     if not args.no_e2e:
-        line["e2e"] = run_e2e(args, vi, means, conf, views, total_views, world, dist if world > 1 else None, device)
+        dd = dist if world > 1 else None
+        line["e2e"] = run_e2e(args, vi, means, conf, views, total_views, world, dd, device)
+        line["e2e"]["full_state"] = run_e2e(args, vi, means, conf, views, total_views, world, dd, device, full=True)
 
     if world > 1:
         line["multi_gpu_gradient_check"] = gradient_check(world, rank, device, coalesce)
@@ -688,22 +690,35 @@ def run_gaussians(args, flush, device):
                                   "algorithmic_bytes": bwd_bytes}}
 
 
-def run_e2e(args, vi, means, conf, views, total_views, world, dist, device):
-    """Same step through the public API with host inputs: pinned H2D copies of every
-    input (the scene, and dL/dimage per view) and D2H copies of the images and
-    gradients of every step inside the timed region.
+def run_e2e(args, vi, means, conf, views, total_views, world, dist, device, full=False):
+    """Same step through the public API with host inputs, copies inside the timed region.
+
+    Default (a training step's data path): the scene's parameters are the model
+    and stay on the device; every step copies its inputs from pinned host
+    memory -- each view's camera (view and projection matrices, camera
+    position) and its dL/dimage, which stands for the image a loss compares
+    against -- and reads its result, each view's rendered colour image, back
+    to pinned host memory.  full=True copies the whole scene in and every
+    image and gradient out each step instead (the model round-trips through
+    the host).
 
     The steps are pipelined as a training loop's data path would be: step i+1's
     inputs are copied on a copy stream into the second of two device input sets
     while step i computes, and step i's results are read back on a third stream
     while step i+1 computes (results are recorded on that stream, so the caching
     allocator does not hand their memory out before the read finishes)."""
+    import dataclasses
     from volume_integration.distributed import allreduce_gradients
     s = views[0][0]
-    scene = [t.detach().cpu().pin_memory() for t in (means, conf, s.feature_table, s.linear_weights, s.linear_bias)]
-    per_view = [[t.detach().cpu().pin_memory() for t in (gc, gf)] for _, gc, gf in views]
+    model = [means, conf, s.feature_table, s.linear_weights, s.linear_bias]
+    scene = [t.detach().cpu().pin_memory() for t in model] if full else []
+    per_view = [[t.detach().cpu().pin_memory() for t in (gc, gf)] +
+                ([] if full else [sv.viewmatrix.cpu().pin_memory(), sv.projmatrix.cpu().pin_memory(),
+                                  sv.cam_pos.cpu().pin_memory()])
+                for sv, gc, gf in views]
     slots = [([torch.empty_like(t, device=device) for t in scene],
               [[torch.empty_like(t, device=device) for t in pv] for pv in per_view]) for _ in range(2)]
+    resident = [t.detach().clone() for t in model] if not full else None
     h2d = sum(t.numel() * t.element_size() for t in scene) + \
         sum(t.numel() * t.element_size() for pv in per_view for t in pv)
     comp = torch.cuda.current_stream()
@@ -727,17 +742,21 @@ def run_e2e(args, vi, means, conf, views, total_views, world, dist, device):
         nonlocal outs
         dev_scene, dev_views = slots[k]
         comp.wait_event(h2d_ev[k])
-        m, c, t, w, b = dev_scene
+        m, c, t, w, b = dev_scene if full else resident
         for x in (c, t, w, b):
             x.requires_grad_(True)
         res, acc = [], None
-        for (sv, _, _), (gc, gf) in zip(views, dev_views):
+        for (sv, _, _), dv in zip(views, dev_views):
+            gc, gf = dv[0], dv[1]
+            if not full:
+                sv = dataclasses.replace(sv, viewmatrix=dv[2], projmatrix=dv[3], cam_pos=dv[4])
             oc, of, vis = vi.integrate_primitives(m, c, t, w, b, sv)
             grads = torch.autograd.grad([oc, of], [c, t, w, b], [gc, gf])
             acc = list(grads) if acc is None else [a.add_(g) for a, g in zip(acc, grads)]
-            res += [oc.detach(), of.detach(), vis.detach()]
+            res += [oc.detach(), of.detach(), vis.detach()] if full else [oc.detach()]
         allreduce_gradients(acc)
-        res += acc
+        if full:
+            res += acc
         for x in (c, t, w, b):
             x.requires_grad_(False)
         done_ev[k].record(comp)
@@ -776,6 +795,9 @@ def run_e2e(args, vi, means, conf, views, total_views, world, dist, device):
     d2h = sum(o.numel() * o.element_size() for o in outs)
     return {"value": round(total_views * args.steps / (ms / 1000.0), 3), "unit": "frames/s",
             "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+            "copies": ("every parameter of the scene in; images and gradients out" if full else
+                       "each view's camera and dL/dimage in; each view's colour image out; parameters and "
+                       "gradients stay on the device"),
             "pipelined": "inputs of step i+1 copied and results of step i read back while step i / i+1 compute"}
 
 
