@@ -79,3 +79,36 @@ def test_withheld_tile_hook_rejects_single_tile_and_bad_limits():
                                            ctypes.byref(st), stream) == 1
     assert lib.vi_sort_pairs_withheld_tile(_p(keys), _p(vals), _p(keys), _p(vals), n, 0, 64, _p(temp), tb, 0,
                                            ctypes.byref(st), stream) == 1
+
+
+def test_render_staging_wait_gives_up_and_is_reported(monkeypatch):
+    # The render's bulk copies complete on an mbarrier that every pixel waits
+    # for, at most a bounded number of polls.  The testing hook withholds each
+    # batch's barrier arrival and copies, so nothing completes the wait (and
+    # nothing is in flight): every tile must give up, latch
+    # VI_DEVICE_STAGE_TIMEOUT, read the records
+    # from global memory instead, and produce exactly the images of a normal
+    # run.  With debug on, the forward reports the bit as an error.
+    import vi_testlib as tl
+    VI_DEVICE_STAGE_TIMEOUT = 0x4
+    means, conf, s = tl.custom_scene(seed=21, P=400)
+    s.debug = False
+    ok = tl.gpu_state(means, conf, s)
+    assert not ok["status"][0] & VI_DEVICE_STAGE_TIMEOUT
+    monkeypatch.setenv("VI_RENDER_TMA_TEST_TIMEOUT", "1")
+    to = tl.gpu_state(means, conf, s)
+    assert to["status"][0] & VI_DEVICE_STAGE_TIMEOUT
+    for k in ("n_contrib", "final_T", "contrib_idx", "delta_t", "contrib_rec"):
+        np.testing.assert_array_equal(to[k], ok[k])
+    g_to = tl.run_gpu(means, conf, s, state=False)
+    monkeypatch.delenv("VI_RENDER_TMA_TEST_TIMEOUT")
+    g_ok = tl.run_gpu(means, conf, s, state=False)
+    for k in ("out_color", "out_features", "visibility"):
+        np.testing.assert_array_equal(g_to[k], g_ok[k])
+    # debug: the status word is read after the render and raises
+    monkeypatch.setenv("VI_RENDER_TMA_TEST_TIMEOUT", "1")
+    s.debug = True
+    with pytest.raises(RuntimeError, match="0x4"):
+        tl.run_gpu(means, conf, s, state=False)
+    monkeypatch.delenv("VI_RENDER_TMA_TEST_TIMEOUT")
+    torch.cuda.synchronize()

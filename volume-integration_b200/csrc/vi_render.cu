@@ -56,7 +56,8 @@ __global__ void __launch_bounds__(VI_TILE_PIX, STAGE ? 4 : 1) render_kernel(Scen
                                                             float* __restrict__ delta_t,
                                                             uint32_t* __restrict__ contrib_rec,
                                                             float* __restrict__ trans, uint32_t* __restrict__ trig,
-                                                            uint32_t* __restrict__ status) {
+                                                            uint32_t* __restrict__ status, int stage_wait_limit,
+                                                            bool stage_withhold) {
   __shared__ unsigned long long mask[VI_TILE_PIX];
   __shared__ uint8_t slot[VI_TILE_PIX * kBatch];
   __shared__ uint32_t ent_rec[kBatch];
@@ -234,17 +235,17 @@ __global__ void __launch_bounds__(VI_TILE_PIX, STAGE ? 4 : 1) render_kernel(Scen
         if (tid == 0) {
           const int use = stage_live && total > 0u && total <= (uint32_t)kRows;
           stage_use = use;
-          if (use) mbar_arrive_expect_tx(&mbar, total * OMAX * (uint32_t)sizeof(float));
+          if (use && !stage_withhold) mbar_arrive_expect_tx(&mbar, total * OMAX * (uint32_t)sizeof(float));
         }
       }
       __syncthreads();
       if (stage_use) {
-        if (tid < nb && ent_cnt[tid] > 0u) {
+        if (!stage_withhold && tid < nb && ent_cnt[tid] > 0u) {
           fence_proxy_async_smem();
           bulk_copy_g2s(stage + ent_off[tid] * OMAX, rec_props + (size_t)ent_rec[tid] * OMAX,
                         ent_cnt[tid] * OMAX * (uint32_t)sizeof(float), &mbar);
         }
-        use_stage = mbar_wait(&mbar, phase, kStageWaitLimit);
+        use_stage = mbar_wait(&mbar, phase, stage_wait_limit);
         phase ^= 1u;
         if (!use_stage) {
           stage_live = 0;  // read global memory from here on
@@ -290,7 +291,7 @@ __global__ void __launch_bounds__(VI_TILE_PIX, STAGE ? 4 : 1) render_kernel(Scen
   if constexpr (STAGE) {
     // a wait that gave up may leave its copies in flight: give them a bounded
     // time to land before the block's shared memory is released
-    if (tid == 0 && !stage_live) mbar_wait(&mbar, phase ^ 1u, kStageWaitLimit);
+    if (tid == 0 && !stage_live) mbar_wait(&mbar, phase ^ 1u, stage_wait_limit);
   }
   if (!inside) return;
   if (has_p && T >= 1e-4f && cnt < K) {
@@ -322,13 +323,21 @@ void launch_render(const Scene& sc, const GeomState& g, const uint32_t* point_li
   // build's unstaged form (0.480 ms for an earlier unstaged build).
   const char* e = std::getenv("VI_RENDER_TMA");
   const bool stage = !(e && e[0] == '0') && sc.V <= 32;
+  // Testing hook for the bounded wait (VI_RENDER_TMA_TEST_TIMEOUT=1): the
+  // batches' barrier arrival and copies are withheld, so nothing completes the
+  // phase every pixel waits on (and nothing is in flight); each tile gives up
+  // after 256 polls, latches VI_ERR_STAGE_TIMEOUT and reads global memory,
+  // with the same results.
+  const char* t = std::getenv("VI_RENDER_TMA_TEST_TIMEOUT");
+  const bool test_timeout = t && t[0] == '1';
+  const int wait_limit = test_timeout ? 256 : kStageWaitLimit;
   auto k = sc.O > 8 ? (sc.V > 32 ? render_kernel<16, true, false>
                                  : (stage ? render_kernel<16, false, true> : render_kernel<16, false, false>))
                     : (sc.V > 32 ? render_kernel<8, true, false>
                                  : (stage ? render_kernel<8, false, true> : render_kernel<8, false, false>));
   k<<<tiles, VI_TILE_PIX, 0, s>>>(sc, point_list, im.ranges, g.depths, g.rec_cnt, g.rec_key, g.rec_props, out_color,
                                   out_feat, vis, im.final_T, im.n_contrib, im.contrib_idx, im.delta_t, im.contrib_rec,
-                                  im.trans, im.trig, g.status);
+                                  im.trans, im.trig, g.status, wait_limit, test_timeout);
 }
 
 }  // namespace vi
