@@ -362,15 +362,14 @@ def run_ours(args):
         # as seen from the slowest rank (the others also wait for it there)
         comp = sum(a.elapsed_time(m) for (a, _), m in zip(ev, mid_ev)) / args.steps
         ar = sum(m.elapsed_time(b) for (_, b), m in zip(ev, mid_ev)) / args.steps
-        cmax = torch.tensor([comp], device=device)
-        cmin = torch.tensor([comp], device=device)
-        dist.all_reduce(cmax, op=dist.ReduceOp.MAX)
-        dist.all_reduce(cmin, op=dist.ReduceOp.MIN)
-        slow = torch.tensor([ar if comp >= float(cmax.item()) - 1e-9 else 1e9], device=device)
-        dist.all_reduce(slow, op=dist.ReduceOp.MIN)
-        breakdown = {"compute_ms_max_rank": round(float(cmax.item()), 4),
-                     "compute_ms_min_rank": round(float(cmin.item()), 4),
-                     "allreduce_ms_slowest_rank": round(float(slow.item()), 4),
+        mine = torch.tensor([comp, ar], dtype=torch.float64, device=device)
+        every = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(every, mine)
+        per_rank = [tuple(x.tolist()) for x in every]
+        slowest = max(range(world), key=lambda r: per_rank[r][0])
+        breakdown = {"compute_ms_max_rank": round(per_rank[slowest][0], 4),
+                     "compute_ms_min_rank": round(min(c for c, _ in per_rank), 4),
+                     "allreduce_ms_slowest_rank": round(per_rank[slowest][1], 4),
                      "allreduce": "one flat buffer" if coalesce else "one all-reduce per gradient tensor",
                      "gradient_bytes": int(sum(x.numel() * x.element_size() for x in acc))}
         dist.barrier()
