@@ -270,3 +270,13 @@ def test_render_without_record_staging(name, monkeypatch):
     monkeypatch.setenv("VI_RENDER_TMA", "0")
     means, conf, s = tl.custom_scene(seed=zlib.crc32(name.encode()) % 1000, **CUSTOM[name])
     _check(means, conf, s, seed=3)
+
+
+@pytest.mark.parametrize("name", ["default", "grid5", "T_not_pow2", "F4L16_D64", "dense_levels"])
+def test_feature_stage_on_callers_table_layout(name, monkeypatch):
+    # the feature stage reads a level-major copy of the table by default; with
+    # VI_TABLE_LAYOUT=entry (read at every forward) it reads the caller's
+    # entry-major table, with the same results
+    monkeypatch.setenv("VI_TABLE_LAYOUT", "entry")
+    means, conf, s = tl.custom_scene(seed=zlib.crc32(name.encode()) % 1000, **CUSTOM[name])
+    _check(means, conf, s, seed=5)

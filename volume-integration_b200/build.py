@@ -23,7 +23,7 @@ OBJ = os.path.join(HERE, "_build", "obj")
 INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(PKG, "libvi_b200.so")
 SOURCES = ["vi_sort.cu", "vi_binning.cu", "vi_features.cu", "vi_render.cu", "vi_backward.cu", "vi_api.cu",
-           "vi_sort_noalloc.cu", "vi_gaussians.cu"]
+           "vi_sort_noalloc.cu", "vi_gaussians.cu", "vi_table.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -165,7 +165,7 @@ size_t phi_cache_max_bytes() {
   return (end && *end == '\0') ? (size_t)v : kPhiCacheMaxBytes;
 }
 
-GeomState geom_layout(char* base, size_t P, int V, int O, int D) {
+GeomState geom_layout(char* base, size_t P, int V, int O, int D, size_t table_floats) {
   GeomState g;
   Carver c(base);
   const int OP = props_stride(O);
@@ -195,6 +195,8 @@ GeomState geom_layout(char* base, size_t P, int V, int O, int D) {
   cap = std::min(cap, (size_t)kCornerCache - 1);  // the top bit of cls_base marks box-corner primitives
   g.phi_cap = (uint32_t)cap;
   g.phi_cache = c.take<float>(cap * (size_t)D);
+  // After everything the backward reads: only the forward uses it.
+  g.table_lm = table_floats ? c.take<float>(table_floats) : nullptr;
   g.bytes = c.size();
   return g;
 }
@@ -254,6 +256,8 @@ int make_scene(Scene& sc, int P, const float* means3D, const float* conf, float 
   sc.L = (int)L; sc.F = (int)F; sc.D = (int)(L * F); sc.Fout = (int)Fout; sc.O = (int)Fout + 4;
   sc.K = K; sc.genus = genus;
   sc.T = (uint32_t)T;
+  sc.tab_l = F;  // the caller's entry-major layout until a level-major copy replaces it
+  sc.tab_e = L * F;
   sc.Tmask = ((uint32_t)T & ((uint32_t)T - 1)) == 0 ? (uint32_t)T - 1 : 0u;
   sc.scale = scale;
   sc.step = G > 1 ? scale / (float)(G - 1) : scale;  // forward.cu:395
@@ -266,6 +270,7 @@ int make_scene(Scene& sc, int P, const float* means3D, const float* conf, float 
   sc.gx = (unsigned)(W + VI_TILE - 1) / VI_TILE;
   sc.gy = (unsigned)(H + VI_TILE - 1) / VI_TILE;
   sc.exact = false;
+  sc.own_box = hash_bounds != nullptr;
   for (int a = 0; a < 3; a++) {
     if (!hash_bounds) {
       sc.hlo[a] = -1.3f;  // hashgrid.h:225-226
@@ -416,11 +421,12 @@ int forward_impl(
   }
   const size_t tiles = (size_t)sc.gx * sc.gy;
 
-  GeomState g = geom_layout(nullptr, P, sc.V, sc.O, sc.D);
+  const size_t tfl = table_level_major() ? (size_t)sc.T * sc.L * sc.F : 0;
+  GeomState g = geom_layout(nullptr, P, sc.V, sc.O, sc.D, tfl);
   char* gb = geom_buffer(geom_user, g.bytes);
   if (!gb) return fail(VI_ERR_ALLOC, "geometry buffer of %zu bytes", g.bytes);
   if ((uintptr_t)gb & 255) return fail(VI_ERR_INVALID_ARGUMENT, "state buffers must be 256-byte aligned");
-  g = geom_layout(gb, P, sc.V, sc.O, sc.D);
+  g = geom_layout(gb, P, sc.V, sc.O, sc.D, tfl);
   ImgState im = img_layout(nullptr, N, sc.K, tiles, sc.exact);
   char* ib = img_buffer(img_user, im.bytes);
   if (!ib) return fail(VI_ERR_ALLOC, "image buffer of %zu bytes", im.bytes);
@@ -446,6 +452,12 @@ int forward_impl(
   // The feature stage depends only on preprocess: queue it before blocking on
   // the overlap count so the GPU works while the host waits.
   stage_begin(kStFeatures, s);
+  if (g.table_lm) {
+    launch_table_to_level_major(sc.table, g.table_lm, sc.T, sc.L, sc.F, s);
+    sc.table = g.table_lm;
+    sc.tab_l = (size_t)sc.T * sc.F;
+    sc.tab_e = (uint32_t)sc.F;
+  }
   launch_features(sc, g, s);
   stage_end(kStFeatures, s);
   if ((rc = check(s, debug, "features", g.status))) return rc;
@@ -528,7 +540,7 @@ int backward_impl(
   if (((uintptr_t)feature_table) % (size_t)(sc.F >= 4 ? 16 : sc.F * 4) != 0 ||
       ((uintptr_t)dL_dfeature_table) % (size_t)(sc.F >= 4 ? 16 : sc.F * 4) != 0)
     return fail(VI_ERR_INVALID_ARGUMENT, "feature_table and its gradient must be aligned to one entry's vector");
-  GeomState g = geom_layout(geom_buffer, P, sc.V, sc.O, sc.D);
+  GeomState g = geom_layout(geom_buffer, P, sc.V, sc.O, sc.D, 0);  // the caller's table: no level-major copy
   ImgState im = img_layout(img_buffer, N, sc.K, (size_t)sc.gx * sc.gy, sc.exact);
   const uint32_t* point_list = nullptr;
   if (sc.exact) {
@@ -694,7 +706,7 @@ extern "C" int vi_get_state_layout(int P, int64_t num_rendered, int image_height
   const int V = grid_size * grid_size * grid_size, O = (int)output_feature_dim + 4;
   const size_t N = (size_t)image_width * image_height;
   const size_t tiles = (size_t)((image_width + 15) / 16) * ((image_height + 15) / 16);
-  GeomState g = geom_layout(nullptr, P, V, O, 0);
+  GeomState g = geom_layout(nullptr, P, V, O, 0, 0);
   const int tb = tile_bits(tiles);
   BinState b = bin_layout(nullptr, (uint64_t)num_rendered, tb);
   ImgState m = img_layout(nullptr, N, max_primitives_per_ray, tiles, false);
@@ -724,7 +736,7 @@ extern "C" int vi_get_state_layout(int P, int64_t num_rendered, int image_height
 }
 
 extern "C" int vi_read_device_status(const char* geom_buffer, uint32_t* status, void* stream) {
-  GeomState g = geom_layout((char*)geom_buffer, 0, 1, 4, 0);
+  GeomState g = geom_layout((char*)geom_buffer, 0, 1, 4, 0, 0);
   cudaError_t e = cudaMemcpyAsync(status, g.status, 4, cudaMemcpyDeviceToHost, (cudaStream_t)stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
   return e == cudaSuccess ? VI_OK : cuda_fail(e, "read status");

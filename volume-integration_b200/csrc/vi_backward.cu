@@ -491,6 +491,124 @@ __device__ __forceinline__ void scatter_level(const LevelCorners& c, float* __re
   }
 }
 
+// Sum over the warp of v[idx] for this lane's idx = lane >> (5 - log2 NV):
+// recursive halving (each lane keeps half of its values and adds its partner's
+// copy of that half), then butterflies over the remaining lane bits.  NV - 1 +
+// (5 - log2 NV) shuffles in all; the whole warp calls it.
+template <int NV>
+__device__ __forceinline__ float warp_reduce_scatter(float* v, uint32_t lane) {
+  constexpr int LOG = NV == 8 ? 3 : NV == 16 ? 4 : 5;
+  static_assert(NV == 8 || NV == 16 || NV == 32, "8, 16 or 32 values");
+#pragma unroll
+  for (int s = 0; s < 5; s++) {
+    const int b = 16 >> s;
+    if (s < LOG) {
+      const int h = NV >> (s + 1);
+      const bool up = (lane & (uint32_t)b) != 0u;
+#pragma unroll
+      for (int i = 0; i < h; i++) {
+        const float send = up ? v[i] : v[i + h];
+        const float keep = up ? v[i + h] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, b);
+      }
+    } else {
+      v[0] += __shfl_xor_sync(0xffffffffu, v[0], b);
+    }
+  }
+  return v[0];
+}
+
+// scatter_level for a warp whose lanes query one level: when every lane that
+// scatters (`on`) lies in the same hashgrid cell, the eight corners' terms
+// A[f] * (corner weight) are summed over the warp first and each (corner,
+// feature) takes one atomic instead of one per lane (a primitive's grid points
+// lie in one cell at the coarse levels whenever the box is not much larger than
+// the scene).  Otherwise every lane scatters its own corners.  The whole warp
+// calls it; the atomics add the same terms, only their grouping differs.
+template <int F, bool POW2>
+__device__ __forceinline__ void scatter_level_warp(bool on, const LevelCorners& c, float* __restrict__ dst,
+                                                   uint32_t stride, uint32_t T, uint32_t Tmask, const float* A,
+                                                   uint32_t lane) {
+  const uint32_t onm = __ballot_sync(0xffffffffu, on);
+  if (onm == 0u) return;
+  const int lead = __ffs(onm) - 1;
+  const uint32_t x0 = __shfl_sync(0xffffffffu, c.ix0, lead), y0 = __shfl_sync(0xffffffffu, c.iy0, lead),
+                 z0 = __shfl_sync(0xffffffffu, c.iz0, lead);
+  const bool same = !on || (c.ix0 == x0 && c.iy0 == y0 && c.iz0 == z0);
+  if constexpr (F == 1 || F == 2 || F == 4) {
+    if (__all_sync(0xffffffffu, same)) {
+      constexpr int NV = 8 * F;
+      float v[NV];
+      const float wxy[4] = {c.wx0 * c.wy0, c.wx0 * c.wy1, c.wx1 * c.wy0, c.wx1 * c.wy1};
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        const bool use = on && ((c.mask >> k) & 1u);
+        const float w = wxy[k >> 1] * ((k & 1) ? c.wz1 : c.wz0);
+#pragma unroll
+        for (int f = 0; f < F; f++) v[k * F + f] = use ? A[f] * w : 0.0f;
+      }
+      const float sum = warp_reduce_scatter<NV>(v, lane);
+      const uint32_t um = __reduce_or_sync(0xffffffffu, on ? c.mask : 0u);
+      // the shared cell's corner indices (the lead lane's)
+      const uint32_t x1 = __shfl_sync(0xffffffffu, c.ix1, lead), y1 = __shfl_sync(0xffffffffu, c.iy1, lead),
+                     z1 = __shfl_sync(0xffffffffu, c.iz1, lead);
+      const bool hsh = __shfl_sync(0xffffffffu, c.hsh ? 1 : 0, lead) != 0;
+      constexpr int SH = NV == 8 ? 2 : NV == 16 ? 1 : 0;  // lanes holding one sum: lane % 2^SH == 0
+      if ((lane & ((1u << SH) - 1u)) == 0u) {
+        const int idx = (int)(lane >> SH), k = idx / F, f = idx - k * F;
+        if ((um >> k) & 1u) {
+          const uint32_t x = (k & 4) ? x1 : x0, y = (k & 2) ? y1 : y0, z = (k & 1) ? z1 : z0;
+          uint32_t e;
+          if (hsh) {
+            const uint32_t h = x ^ y ^ z;
+            e = POW2 ? (h & Tmask) : (h % T);
+          } else {
+            e = x + y + z;
+          }
+          atomicAdd(dst + (size_t)e * stride + f, sum);
+        }
+      }
+      return;
+    }
+  }
+  if (on) scatter_level<F, POW2>(c, dst, stride, T, Tmask, A);
+}
+
+// The table-gradient scatter of a primitive with more than 16 position
+// classes, all cached: one class per lane, every lane on the same level, so
+// each level's scatter is summed over the warp when the classes share a cell
+// (scatter_level_warp).
+template <int F, int OMAX>
+__device__ __forceinline__ void scatter_classes_warp(const float* W_s, const float* S_s, const uint32_t* mem_s,
+                                                  const float4* npos_s, const int* res_s, const float* resf_s,
+                                                  const int* hash_s, uint32_t p0, uint32_t p1, uint32_t p2,
+                                                  uint32_t T, uint32_t Tmask, int L, int DP, int U, uint32_t amask,
+                                                  float* __restrict__ dtable, uint32_t stride, uint32_t lane) {
+  const bool cl = (int)lane < U;
+  const bool on = cl && (mem_s[cl ? lane : 0] & amask) != 0u;
+  const float4 n4 = npos_s[cl ? lane : 0];
+  const float3 nn = make_float3(n4.x, n4.y, n4.z);
+  float S[OMAX];
+#pragma unroll
+  for (int o = 0; o < OMAX; o++) S[o] = on ? S_s[lane * OMAX + o] : 0.0f;
+  for (int l = 0; l < L; l++) {
+    const LevelCorners lc = level_corners(nn, res_s[l], resf_s[l], hash_s[l] != 0, p0, p1, p2, T);
+    float A[F];
+#pragma unroll
+    for (int f = 0; f < F; f++) {
+      float sum = 0.0f;
+#pragma unroll
+      for (int o = 0; o < OMAX; o++) sum += W_s[o * DP + l * F + f] * S[o];
+      A[f] = sum;
+    }
+    float* dst = dtable + (size_t)l * F;
+    if (Tmask)
+      scatter_level_warp<F, true>(on, lc, dst, stride, T, Tmask, A, lane);
+    else
+      scatter_level_warp<F, false>(on, lc, dst, stride, T, Tmask, A, lane);
+  }
+}
+
 // One warp per primitive, lane g = grid point g.  With dIn_p = W^T dpre_p
 // (backward.cu:608-619), every per-pair sum collapses onto O-wide vectors:
 //   v_g  = sum_p g'_{p,g} dpre_p                 -> dconf_g = v_g . (W phi_g)
@@ -500,11 +618,18 @@ __device__ __forceinline__ void scatter_level(const LevelCorners& c, float* __re
 // corners, so conf*vA and E are summed per position class; the hashgrid gather
 // (for phi) and scatter (for the table gradient) then run once per (class,
 // level), spread over the warp's lanes.
+// WARP: primitives with more than 16 position classes, all cached, sum each
+// level's table-gradient scatter over the warp (scatter_classes_warp).  It is a
+// separate instance, taken when the caller sets the hashgrid box: inside the
+// scene's own bounds every grid point is a class and the points of one
+// primitive share cells at most levels, while with the reference's fixed box
+// few primitives have that many classes, and this kernel's loop measured 20%
+// slower with the extra path in it (its instruction fetch stalls grew eightfold).
 // EXACT: the exact-gradient mode (see backward_pixel_exact_kernel): grid points
 // join records by the forward projection, dconf = mag (W phi) . dpre for the
 // grid points that form the record, the table coefficient of a class is
 // W^T (sum of E), and dL/dmeans3D gains the hashgrid's spatial derivative.
-template <int F, int OMAX, bool EXACT>
+template <int F, int OMAX, bool EXACT, bool WARP>
 __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene sc, GeomState g, float* __restrict__ dmeans,
                                                                       float* __restrict__ dconf,
                                                                       float* __restrict__ dtable, float* __restrict__ dW) {
@@ -799,7 +924,11 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
     // level that hit the same table entry share one request.
     const LevelWalk it(pc.U, L);
     float dpos[3] = {0.0f, 0.0f, 0.0f};
-    for (int l0 = corner ? L : 0; l0 < L; l0 += it.per) {
+    const bool warp_scatter = WARP && !EXACT && cached && !corner && pc.U > 16;
+    if (warp_scatter)
+      scatter_classes_warp<F, OMAX>(W_s, S_s, mem_s, npos_s, res_s, resf_s, hash_s, p0, p1, p2, sc.T, sc.Tmask, L,
+                                    DP, pc.U, amask, dtable, stride, lane);
+    for (int l0 = (corner || warp_scatter) ? L : 0; l0 < L; l0 += it.per) {
       if (!it.valid(l0)) continue;
       const int l = it.level(l0), u = it.u;
       const bool doA = (mem_s[u] & (EXACT ? emask : amask)) != 0u;
@@ -1125,7 +1254,9 @@ void launch_prim_t(const Scene& sc, GeomState& g, float* dmeans, float* dconf, f
   }
   const int D = sc.L * F;
   size_t smem = sizeof(float) * (bwd_head_floats(D, sc.L, OMAX) + kBwdWarps * bwd_warp_floats(D, OMAX));
-  auto k = sc.exact ? backward_prim_kernel<F, OMAX, true> : backward_prim_kernel<F, OMAX, false>;
+  auto k = sc.exact     ? backward_prim_kernel<F, OMAX, true, false>
+           : sc.own_box ? backward_prim_kernel<F, OMAX, false, true>
+                        : backward_prim_kernel<F, OMAX, false, false>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   cudaMemsetAsync(g.status + 5, 0, sizeof(uint32_t), s);
   // A resident grid: warps draw primitives from the counter until it runs out.

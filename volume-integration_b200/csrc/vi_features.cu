@@ -71,7 +71,7 @@ __global__ void __launch_bounds__(kFeatWarps * 32, 3) features_kernel(Scene sc, 
   __syncthreads();
   {
     const uint32_t c0 = (uint32_t)__ldg(sc.primes), c1 = (uint32_t)__ldg(sc.primes + 1), c2 = (uint32_t)__ldg(sc.primes + 2);
-    box_corner_features<F>(sc, res_s, resf_s, hash_s, c0, c1, c2, DP, cphi_s);
+    box_corner_features<F, true, POW2 ? 1 : 0>(sc, res_s, resf_s, hash_s, c0, c1, c2, DP, cphi_s);
     for (int t = threadIdx.x; t < 8 * OMAX; t += blockDim.x) {
       const int c = t / OMAX, o = t % OMAX;
       float acc = 0.0f;
@@ -86,7 +86,7 @@ __global__ void __launch_bounds__(kFeatWarps * 32, 3) features_kernel(Scene sc, 
   const uint32_t lt_mask = (1u << lane) - 1;
   const uint32_t p0 = (uint32_t)__ldg(sc.primes), p1 = (uint32_t)__ldg(sc.primes + 1),
                  p2 = (uint32_t)__ldg(sc.primes + 2);
-  const uint32_t stride = (uint32_t)D;
+  const uint32_t stride = sc.tab_e;
   const int OP = OMAX;
   // Warps claim chunks of 32 consecutive primitives from a counter (status[4]):
   // the cost of a primitive varies widely, so a fixed share per warp would
@@ -162,11 +162,11 @@ __global__ void __launch_bounds__(kFeatWarps * 32, 3) features_kernel(Scene sc, 
           for (int f = 0; f < F; f++) acc0[f] = acc1[f] = 0.0f;
           if (v0) {
             const LevelCorners lc = level_corners(nn, res_s[la], resf_s[la], hash_s[la] != 0, p0, p1, p2, sc.T);
-            gather_level<F, POW2>(lc, sc.table + (size_t)la * F, stride, sc.T, sc.Tmask, acc0);
+            gather_level<F, POW2>(lc, sc.table + (size_t)la * sc.tab_l, stride, sc.T, sc.Tmask, acc0);
           }
           if (v1) {
             const LevelCorners lc = level_corners(nn, res_s[lb], resf_s[lb], hash_s[lb] != 0, p0, p1, p2, sc.T);
-            gather_level<F, POW2>(lc, sc.table + (size_t)lb * F, stride, sc.T, sc.Tmask, acc1);
+            gather_level<F, POW2>(lc, sc.table + (size_t)lb * sc.tab_l, stride, sc.T, sc.Tmask, acc1);
           }
           if (v0) {
 #pragma unroll
@@ -359,7 +359,7 @@ __global__ void __launch_bounds__(kWideThreads) features_wide_kernel(Scene sc, G
 #pragma unroll
         for (int f = 0; f < F; f++) acc[f] = 0.0f;
         const LevelCorners lc = level_corners(n, res_s[l], resf_s[l], hash_s[l] != 0, p0, p1, p2, sc.T);
-        gather_level<F, POW2>(lc, sc.table + (size_t)l * F, (uint32_t)D, sc.T, sc.Tmask, acc);
+        gather_level<F, POW2>(lc, sc.table + (size_t)l * sc.tab_l, sc.tab_e, sc.T, sc.Tmask, acc);
 #pragma unroll
         for (int f = 0; f < F; f++) phi[l * F + f] = acc[f];
       }

@@ -101,6 +101,7 @@ struct GeomState {
   uint32_t* cls_base;        // [P] first slot of the primitive's position classes in phi_cache, or kNoCache
   float* phi_cache;          // [phi_cap][D] hashgrid features of each position class (feature stage)
   uint32_t phi_cap;          // slots in phi_cache
+  float* table_lm;           // [L][T][F] the feature stage's level-major copy of the table (forward only; else null)
   size_t bytes;
 };
 constexpr uint32_t kNoCache = 0xffffffffu;
@@ -111,12 +112,22 @@ constexpr uint32_t kCornerCache = 0x80000000u;
 // fits, else this many bytes (primitives that find no room gather in the
 // backward).  The environment variable VI_PHI_CACHE_BYTES overrides it (0 turns
 // the cache off); it is read at every call, and the backward does not need the
-// value the forward used, since phi_cache is the last array of the layout.
+// value the forward used, since phi_cache is the last array the backward reads.
 constexpr size_t kPhiCacheMaxBytes = 8ull << 30;
 size_t phi_cache_max_bytes();
 constexpr uint32_t kBwdDiffers = 0x80000000u;
 constexpr int kScanBlock = 2048;
-GeomState geom_layout(char* base, size_t P, int V, int O, int D);
+// table_floats: T*L*F when the feature stage reads a level-major copy of the
+// table (the forward), else 0.  The copy is the layout's last array, so the
+// backward, which does not read it, lays the buffer out with 0.
+GeomState geom_layout(char* base, size_t P, int V, int O, int D, size_t table_floats);
+
+// Whether the feature stage reads a level-major copy [L][T][F] of the caller's
+// entry-major table [T][L][F] (VI_TABLE_LAYOUT=entry turns it off; read at every
+// forward).  The backward reads the caller's table and scatters into the
+// caller's gradient.
+bool table_level_major();
+void launch_table_to_level_major(const float* src, float* dst, uint32_t T, int L, int F, cudaStream_t s);
 
 // Binning state: everything sized by the overlap count R.
 struct BinState {
@@ -166,6 +177,13 @@ struct Scene {
   unsigned gx, gy;
   float hlo[3], hext[3];  // hashgrid box: lower corner and extent per axis (reference: -1.3, 2.6)
   bool exact;             // exact-gradient mode (VI_FLAG_EXACT_GRADIENTS)
+  bool own_box;           // the caller set the hashgrid box (hash_bounds), else the reference's fixed box
+  // Addressing of `table`: the features of (entry e, level l) start at
+  // l * tab_l + e * tab_e floats.  The caller's entry-major layout (read by the
+  // backward): tab_l = F, tab_e = L*F; the feature stage's level-major copy:
+  // tab_l = T*F, tab_e = F.
+  size_t tab_l;
+  uint32_t tab_e;
 };
 
 void launch_preprocess(const Scene& sc, GeomState& g, cudaStream_t s);

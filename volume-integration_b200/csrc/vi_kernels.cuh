@@ -225,7 +225,10 @@ __device__ __forceinline__ float3 box_corner_pos(int c) {
   return make_float3((float)((c >> 2) & 1), (float)((c >> 1) & 1), (float)(c & 1));
 }
 // cphi[c * DP + l * F + f] for the 8 corners; the whole block, ends with a barrier.
-template <int F>
+// STRIDES: address the table through sc.tab_l / sc.tab_e (the feature stage's
+// level-major copy); otherwise it is the caller's entry-major table.  POW2: 1 if
+// the table size is a power of two (sc.Tmask != 0), 0 if not, -1 to test it here.
+template <int F, bool STRIDES = false, int POW2 = -1>
 __device__ void box_corner_features(const Scene& sc, const int* res_s, const float* resf_s, const int* hash_s,
                                     uint32_t p0, uint32_t p1, uint32_t p2, int DP, float* cphi) {
   const int L = sc.L;
@@ -235,11 +238,12 @@ __device__ void box_corner_features(const Scene& sc, const int* res_s, const flo
     float acc[F];
 #pragma unroll
     for (int f = 0; f < F; f++) acc[f] = 0.0f;
-    const float* lvl = sc.table + (size_t)l * F;
-    if (sc.Tmask)
-      gather_level<F, true>(lc, lvl, (uint32_t)(L * F), sc.T, sc.Tmask, acc);
+    const float* lvl = sc.table + (size_t)l * (STRIDES ? sc.tab_l : (size_t)F);
+    const uint32_t stride = STRIDES ? sc.tab_e : (uint32_t)(L * F);
+    if (POW2 == 1 || (POW2 < 0 && sc.Tmask))
+      gather_level<F, true>(lc, lvl, stride, sc.T, sc.Tmask, acc);
     else
-      gather_level<F, false>(lc, lvl, (uint32_t)(L * F), sc.T, sc.Tmask, acc);
+      gather_level<F, false>(lc, lvl, stride, sc.T, sc.Tmask, acc);
 #pragma unroll
     for (int f = 0; f < F; f++) cphi[c * DP + l * F + f] = acc[f];
   }
