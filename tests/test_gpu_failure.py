@@ -93,6 +93,7 @@ def test_render_staging_wait_gives_up_and_is_reported(monkeypatch):
     VI_DEVICE_STAGE_TIMEOUT = 0x4
     means, conf, s = tl.custom_scene(seed=21, P=400)
     s.debug = False
+    monkeypatch.setenv("VI_RENDER_TMA", "1")  # the staged render, without the hook
     ok = tl.gpu_state(means, conf, s)
     assert not ok["status"][0] & VI_DEVICE_STAGE_TIMEOUT
     monkeypatch.setenv("VI_RENDER_TMA_TEST_TIMEOUT", "1")

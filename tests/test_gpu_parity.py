@@ -264,10 +264,11 @@ def test_feature_cache_fallback(limit, monkeypatch):
 
 
 @pytest.mark.parametrize("name", ["default", "dense_overlap", "fout8_o12", "K3"])
-def test_render_without_record_staging(name, monkeypatch):
-    # the render's bulk-copy staging of records is the default; the unstaged
-    # form (VI_RENDER_TMA=0, read at every launch) must give the same results
-    monkeypatch.setenv("VI_RENDER_TMA", "0")
+def test_render_with_record_staging(name, monkeypatch):
+    # the render reads records from global memory by default; the form that
+    # stages each batch's records with bulk copies (VI_RENDER_TMA=1, read at
+    # every launch) must give the same results
+    monkeypatch.setenv("VI_RENDER_TMA", "1")
     means, conf, s = tl.custom_scene(seed=zlib.crc32(name.encode()) % 1000, **CUSTOM[name])
     _check(means, conf, s, seed=3)
 

@@ -43,7 +43,7 @@ constexpr int kStageWaitLimit = 1 << 20;
 // after kStageWaitLimit polls latches VI_ERR_STAGE_TIMEOUT and ends staging
 // for the tile.
 template <int OMAX, bool WIDE, bool STAGE>
-__global__ void __launch_bounds__(VI_TILE_PIX, STAGE ? 4 : 1) render_kernel(Scene sc, const uint32_t* __restrict__ point_list,
+__global__ void __launch_bounds__(VI_TILE_PIX, 4) render_kernel(Scene sc, const uint32_t* __restrict__ point_list,
                                                             const uint32_t* __restrict__ ranges,
                                                             const float* __restrict__ depths,
                                                             const uint32_t* __restrict__ rec_cnt,
@@ -317,19 +317,20 @@ void launch_render(const Scene& sc, const GeomState& g, const uint32_t* point_li
   const unsigned tiles = sc.gx * sc.gy;
   if (tiles == 0) return;
   note_launches(1);
-  // Bulk-copy staging of the records for grids of at most 32 points (on by
-  // default; VI_RENDER_TMA=0 reads the records from global memory instead).
-  // Measured on the headline: 0.486 ms staged against 0.630 ms for this
-  // build's unstaged form (0.480 ms for an earlier unstaged build).
-  const char* e = std::getenv("VI_RENDER_TMA");
-  const bool stage = !(e && e[0] == '0') && sc.V <= 32;
-  // Testing hook for the bounded wait (VI_RENDER_TMA_TEST_TIMEOUT=1): the
-  // batches' barrier arrival and copies are withheld, so nothing completes the
-  // phase every pixel waits on (and nothing is in flight); each tile gives up
-  // after 256 polls, latches VI_ERR_STAGE_TIMEOUT and reads global memory,
-  // with the same results.
+  // Bulk-copy staging of the records for grids of at most 32 points: opt-in
+  // (VI_RENDER_TMA=1).  At equal occupancy (4 blocks per SM) the unstaged form
+  // measured faster: 0.480 against 0.489 ms on the headline scene, 21.6
+  // against 25.5 ms on the 4K stress scene, where batches often hold more
+  // records than the stage buffer.
+  // Testing hook for the bounded wait (VI_RENDER_TMA_TEST_TIMEOUT=1, which
+  // also turns staging on): the batches' barrier arrival and copies are
+  // withheld, so nothing completes the phase every pixel waits on (and nothing
+  // is in flight); each tile gives up after 256 polls, latches
+  // VI_ERR_STAGE_TIMEOUT and reads global memory, with the same results.
   const char* t = std::getenv("VI_RENDER_TMA_TEST_TIMEOUT");
   const bool test_timeout = t && t[0] == '1';
+  const char* e = std::getenv("VI_RENDER_TMA");
+  const bool stage = ((e && e[0] == '1') || test_timeout) && sc.V <= 32;
   const int wait_limit = test_timeout ? 256 : kStageWaitLimit;
   auto k = sc.O > 8 ? (sc.V > 32 ? render_kernel<16, true, false>
                                  : (stage ? render_kernel<16, false, true> : render_kernel<16, false, false>))
