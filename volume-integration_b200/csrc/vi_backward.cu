@@ -618,6 +618,8 @@ __device__ __forceinline__ void scatter_classes_warp(const float* W_s, const flo
 // corners, so conf*vA and E are summed per position class; the hashgrid gather
 // (for phi) and scatter (for the table gradient) then run once per (class,
 // level), spread over the warp's lanes.
+// SKIPC: primitives whose grid points all clamp to one box corner are left to
+// backward_corner_kernel (launched after this one).
 // WARP: primitives with more than 16 position classes, all cached, sum each
 // level's table-gradient scatter over the warp (scatter_classes_warp).  It is a
 // separate instance, taken when the caller sets the hashgrid box: inside the
@@ -629,7 +631,7 @@ __device__ __forceinline__ void scatter_classes_warp(const float* W_s, const flo
 // join records by the forward projection, dconf = mag (W phi) . dpre for the
 // grid points that form the record, the table coefficient of a class is
 // W^T (sum of E), and dL/dmeans3D gains the hashgrid's spatial derivative.
-template <int F, int OMAX, bool EXACT, bool WARP>
+template <int F, int OMAX, bool EXACT, bool WARP, bool SKIPC>
 __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene sc, GeomState g, float* __restrict__ dmeans,
                                                                       float* __restrict__ dconf,
                                                                       float* __restrict__ dtable, float* __restrict__ dW) {
@@ -697,6 +699,10 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
     if (q0 >= sc.P) break;
     const uint32_t cnt = (int)lane < kGrab && q0 + (int)lane < sc.P ? g.rec_cnt[q0 + lane] : 0u;
     uint32_t batch = __ballot_sync(0xffffffffu, (cnt & ~kBwdDiffers) != 0u);
+    if (SKIPC) {  // box-corner primitives are backward_corner_kernel's
+      const uint32_t cbx = (int)lane < kGrab && q0 + (int)lane < sc.P ? g.cls_base[q0 + lane] : kNoCache;
+      batch &= ~__ballot_sync(0xffffffffu, cbx != kNoCache && (cbx & kCornerCache) != 0u);
+    }
     while (batch) {
     const int q = q0 + __ffs(batch) - 1;
     batch &= batch - 1;
@@ -1074,6 +1080,225 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 5) backward_prim_kernel(Scene 
   }
 }
 
+// Per-primitive backward of the box-corner primitives (every grid point clamps
+// to one corner cc of the hashgrid box, so every grid point has the features
+// phi_cc of that corner): the reference's formula with the 3-tap stencil, as
+// backward_prim_kernel computes it for such a primitive, without position
+// classes, gathers or a per-primitive linear layer.  One warp per primitive,
+// lane g = grid point g.  Per primitive: v_g, vA_g and E_g over the records
+// (the 3-tap search of backward_prim_kernel), dconf_g = v_g . (W phi_cc) from
+// the block's eight corner vectors W phi_c, and the warp's sums of conf_g vA_g
+// and E_g, added per corner into the block's shared rows with one
+// reduce-scatter.  At the end of the block: the table gradient at each corner's
+// entries (W^T of the summed conf vA, one scatter per corner and level) and
+// dW += sum over corners of (summed E) (x) phi_c.
+constexpr int kCornerWarps = 8;
+__host__ __device__ inline int corner_head_floats(int D, int L, int OMAX) {
+  return OMAX * bwd_dp(D) + 3 * pad4(L) + 8 * bwd_dp(D) + 3 * 8 * OMAX;
+}
+template <int F, int OMAX>
+__global__ void __launch_bounds__(kCornerWarps * 32) backward_corner_kernel(Scene sc, GeomState g,
+                                                                             float* __restrict__ dconf,
+                                                                             float* __restrict__ dtable,
+                                                                             float* __restrict__ dW) {
+  extern __shared__ float4 smem4[];
+  float* smem = reinterpret_cast<float*>(smem4);
+  const int L = sc.L, D = L * F, DP = bwd_dp(D), O = sc.O, V = sc.V, G = sc.G;
+  float* W_s = smem;                                      // [OMAX][DP]
+  float* resf_s = W_s + OMAX * DP;                        // [L]
+  int* res_s = reinterpret_cast<int*>(resf_s + pad4(L));  // [L]
+  int* hash_s = res_s + pad4(L);                          // [L]
+  float* cphi_s = reinterpret_cast<float*>(hash_s + pad4(L));  // [8][DP] box-corner features
+  float* cmlp_s = cphi_s + 8 * DP;  // [8][OMAX] W phi_c
+  float* cS_s = cmlp_s + 8 * OMAX;  // [8][OMAX] sums of conf * vA per corner
+  float* cE_s = cS_s + 8 * OMAX;    // [8][OMAX] sums of E per corner
+  const int w = threadIdx.x >> 5;
+  const uint32_t lane = threadIdx.x & 31;
+  float* S_s = smem + corner_head_floats(D, L, OMAX) + w * 32 * OMAX;  // [32][OMAX] the records' dL/dpre
+
+  for (int i = threadIdx.x; i < OMAX * DP; i += blockDim.x) {
+    const int o = i / DP, d = i % DP;
+    W_s[i] = o < O && d < D ? sc.Wl[o * D + d] : 0.0f;
+  }
+  for (int i = threadIdx.x; i < L; i += blockDim.x) {
+    res_s[i] = sc.res[i];
+    resf_s[i] = (float)sc.res[i];
+    hash_s[i] = sc.do_hash[i];
+  }
+  for (int i = threadIdx.x; i < 16 * OMAX; i += blockDim.x) cS_s[i] = 0.0f;  // cS_s and cE_s
+  __syncthreads();
+  const uint32_t p0 = (uint32_t)__ldg(sc.primes), p1 = (uint32_t)__ldg(sc.primes + 1),
+                 p2 = (uint32_t)__ldg(sc.primes + 2);
+  box_corner_features<F>(sc, res_s, resf_s, hash_s, p0, p1, p2, DP, cphi_s);
+  for (int t = threadIdx.x; t < 8 * OMAX; t += blockDim.x) {
+    const int c = t / OMAX, o = t % OMAX;
+    float acc = 0.0f;
+    for (int i = 0; i < D; i++) acc = __fmaf_rn(W_s[o * DP + i], cphi_s[c * DP + i], acc);
+    cmlp_s[t] = acc;
+  }
+  __syncthreads();
+
+  const Stencil st = make_stencil(sc.genus);
+  const GridPt gpt = grid_point((int)lane < V ? (int)lane : 0, G, sc.gof);
+  const bool act = (int)lane < V;
+  constexpr int kGrab = 8;
+  for (;;) {
+    int q0 = 0;
+    if (lane == 0) q0 = (int)atomicAdd(g.status + 8, (unsigned)kGrab);
+    q0 = __shfl_sync(0xffffffffu, q0, 0);
+    if (q0 >= sc.P) break;
+    const bool in = (int)lane < kGrab && q0 + (int)lane < sc.P;
+    const uint32_t cnt = in ? g.rec_cnt[q0 + lane] : 0u;
+    const uint32_t cbx = in ? g.cls_base[q0 + lane] : kNoCache;
+    uint32_t batch = __ballot_sync(0xffffffffu, (cnt & ~kBwdDiffers) != 0u && cbx != kNoCache &&
+                                                    (cbx & kCornerCache) != 0u);
+    while (batch) {
+      const int qi = __ffs(batch) - 1;
+      batch &= batch - 1;
+      const int q = q0 + qi;
+      const int cc = (int)(__shfl_sync(0xffffffffu, cbx, qi) & 7u);
+      const size_t s0 = (size_t)q * V;
+      const uint32_t rp = act ? g.rec_pix[s0 + lane] : 0u;  // pixel + 1 of each grid point's record, else 0
+      const float conf = act ? sc.conf[s0 + lane] : 0.0f;
+      const uint32_t cm = __ballot_sync(0xffffffffu, rp != 0u);
+      if (cm == 0) continue;
+      const float3 c = make_float3(sc.means[3 * q], sc.means[3 * q + 1], sc.means[3 * q + 2]);
+      const float3 pos = grid_pos_rel(c, gpt.rel, sc.step);
+      const float2 sb = project(pos, sc.proj, sc.W, sc.H, false);  // backward.cu:325
+      const int bx = pix_coord(sb.x), by = pix_coord(sb.y);
+      const int bpix = (act && bx >= 0 && bx < sc.W && by >= 0 && by < sc.H) ? by * sc.W + bx : -1;
+      const uint32_t posm = __ballot_sync(0xffffffffu, act && conf > 0.0f);
+      const float mag = act ? occ_mag(posm, gpt, G, st) : 0.0f;
+      const float wE = (act && conf > 0.0f && mag > 1e-7f) ? fmul(conf, mag) : 0.0f;
+      if ((cm >> lane) & 1u) {
+        const float4* src = reinterpret_cast<const float4*>(g.rec_dpre + (s0 + lane) * OMAX);
+        float4* dstr = reinterpret_cast<float4*>(S_s + lane * OMAX);
+#pragma unroll
+        for (int o4 = 0; o4 < OMAX / 4; o4++) dstr[o4] = src[o4];
+      }
+      __syncwarp();
+      float v[OMAX], vA[OMAX], el[OMAX];
+#pragma unroll
+      for (int o = 0; o < OMAX; o++) v[o] = vA[o] = el[o] = 0.0f;
+      bool hasV = false, hasA = false;
+      // the record of this grid point's own pixel, and E from it
+      int myrec = -1;
+      uint32_t m = cm;
+      while (m) {
+        const int j = __ffs(m) - 1;
+        m &= m - 1;
+        if (bpix == (int)__shfl_sync(0xffffffffu, rp, j) - 1) myrec = j;
+      }
+      const bool hasE = myrec >= 0 && wE != 0.0f;
+      if (hasE) {
+#pragma unroll
+        for (int o = 0; o < OMAX; o++) el[o] = fmul(wE, S_s[myrec * OMAX + o]);
+      }
+      // 3-tap stencil: an axis adds 1/2 to record p exactly when one of the two
+      // neighbours along it lies in p's pixel (backward.cu:654-689)
+      const int GG = G * G, gi = (int)lane;
+      int nb[6];
+      nb[0] = __shfl_sync(0xffffffffu, myrec, (gi + 31) & 31);
+      nb[1] = __shfl_sync(0xffffffffu, myrec, (gi + 1) & 31);
+      nb[2] = __shfl_sync(0xffffffffu, myrec, (gi + 32 - G) & 31);
+      nb[3] = __shfl_sync(0xffffffffu, myrec, (gi + G) & 31);
+      nb[4] = __shfl_sync(0xffffffffu, myrec, (gi + 32 - GG) & 31);
+      nb[5] = __shfl_sync(0xffffffffu, myrec, (gi + GG) & 31);
+      if (!act || gpt.x == 0) nb[0] = -1;
+      if (!act || gpt.x + 1 >= G) nb[1] = -1;
+      if (!act || gpt.y == 0) nb[2] = -1;
+      if (!act || gpt.y + 1 >= G) nb[3] = -1;
+      if (!act || gpt.z == 0) nb[4] = -1;
+      if (!act || gpt.z + 1 >= G) nb[5] = -1;
+#pragma unroll
+      for (int a = 0; a < 3; a++)
+        if (nb[2 * a] == nb[2 * a + 1]) nb[2 * a] = nb[2 * a + 1] = -1;
+#pragma unroll
+      for (int i = 0; i < 6; i++) {
+        if (nb[i] >= 0) {
+          int k = 1;
+#pragma unroll
+          for (int kk = i + 1; kk < 6; kk++)
+            if (nb[kk] == nb[i]) {
+              k++;
+              nb[kk] = -1;
+            }
+          const float gp = 0.5f * (float)k;
+          hasV = true;
+          const bool doA = fabsf(fmul(gp, conf)) > 1e-9f;
+          hasA |= doA;
+          const float4* src = reinterpret_cast<const float4*>(S_s + nb[i] * OMAX);
+#pragma unroll
+          for (int o4 = 0; o4 < OMAX / 4; o4++) {
+            const float4 d = src[o4];
+            const float x0 = gp * d.x, x1 = gp * d.y, x2 = gp * d.z, x3 = gp * d.w;
+            v[4 * o4] += x0; v[4 * o4 + 1] += x1; v[4 * o4 + 2] += x2; v[4 * o4 + 3] += x3;
+            if (doA) {
+              vA[4 * o4] += x0; vA[4 * o4 + 1] += x1; vA[4 * o4 + 2] += x2; vA[4 * o4 + 3] += x3;
+            }
+          }
+        }
+      }
+      __syncwarp();  // S_s reads done before the next primitive stages its records
+      const bool gather = hasE || hasV;
+      if (!__any_sync(0xffffffffu, gather)) continue;
+      if (act) {
+        float dX = 0.0f;
+        if (gather) {
+          const float* mr = cmlp_s + cc * OMAX;
+#pragma unroll
+          for (int o = 0; o < OMAX / 2; o++) dX += v[2 * o] * mr[2 * o] + v[2 * o + 1] * mr[2 * o + 1];
+        }
+        dconf[s0 + lane] = dX;
+      }
+      // sums over the warp of conf * vA and of E, added to corner cc's rows
+      constexpr int NV = 2 * OMAX;
+      float sv[NV];
+#pragma unroll
+      for (int o = 0; o < OMAX; o++) {
+        sv[o] = hasA ? conf * vA[o] : 0.0f;
+        sv[OMAX + o] = el[o];
+      }
+      const float tot = warp_reduce_scatter<NV>(sv, lane);
+      constexpr int SH = NV == 16 ? 1 : 0;  // lanes holding one sum: lane % 2^SH == 0
+      if ((lane & ((1u << SH) - 1u)) == 0u && tot != 0.0f) {
+        const int idx = (int)(lane >> SH);
+        atomicAdd(idx < OMAX ? &cS_s[cc * OMAX + idx] : &cE_s[cc * OMAX + idx - OMAX], tot);
+      }
+    }
+  }
+  __syncthreads();
+  // Table gradient at the box corners: one scatter per (corner, level).
+  const uint32_t stride = (uint32_t)D;
+  for (int t = threadIdx.x; t < 8 * L; t += blockDim.x) {
+    const int c = t / L, l = t - (t / L) * L;
+    bool any = false;
+    for (int o = 0; o < OMAX; o++) any |= cS_s[c * OMAX + o] != 0.0f;
+    if (!any) continue;
+    float A[F];
+#pragma unroll
+    for (int f = 0; f < F; f++) {
+      float sum = 0.0f;
+#pragma unroll
+      for (int o = 0; o < OMAX; o++) sum += W_s[o * DP + l * F + f] * cS_s[c * OMAX + o];
+      A[f] = sum;
+    }
+    const LevelCorners lc = level_corners(box_corner_pos(c), res_s[l], resf_s[l], hash_s[l] != 0, p0, p1, p2, sc.T);
+    if (sc.Tmask)
+      scatter_level<F, true>(lc, dtable + (size_t)l * F, stride, sc.T, sc.Tmask, A);
+    else
+      scatter_level<F, false>(lc, dtable + (size_t)l * F, stride, sc.T, sc.Tmask, A);
+  }
+  // dW += sum_c (E sum of corner c) (x) phi_c
+  for (int i = threadIdx.x; i < O * D; i += blockDim.x) {
+    const int o = i / D, d = i - (i / D) * D;
+    float x = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 8; c++) x += cE_s[c * OMAX + o] * cphi_s[c * DP + d];
+    if (x != 0.0f) atomicAdd(&dW[i], x);
+  }
+}
+
 // Per-primitive backward for grids of more than 32 points (G = 4, 5; the
 // reference allows up to 5, backward.cu:26-33): one block of kWideThreads per
 // primitive, thread g = grid point g, following the reference's formula
@@ -1254,9 +1479,13 @@ void launch_prim_t(const Scene& sc, GeomState& g, float* dmeans, float* dconf, f
   }
   const int D = sc.L * F;
   size_t smem = sizeof(float) * (bwd_head_floats(D, sc.L, OMAX) + kBwdWarps * bwd_warp_floats(D, OMAX));
-  auto k = sc.exact     ? backward_prim_kernel<F, OMAX, true, false>
-           : sc.own_box ? backward_prim_kernel<F, OMAX, false, true>
-                        : backward_prim_kernel<F, OMAX, false, false>;
+  // Box-corner primitives go to backward_corner_kernel (reference formula,
+  // 3-tap stencil, the reference's fixed box: where they are common).
+  const bool split = !sc.exact && !sc.own_box && make_stencil(sc.genus).S == 3;
+  auto k = sc.exact     ? backward_prim_kernel<F, OMAX, true, false, false>
+           : sc.own_box ? backward_prim_kernel<F, OMAX, false, true, false>
+           : split      ? backward_prim_kernel<F, OMAX, false, false, true>
+                        : backward_prim_kernel<F, OMAX, false, false, false>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   cudaMemsetAsync(g.status + 5, 0, sizeof(uint32_t), s);
   // A resident grid: warps draw primitives from the counter until it runs out.
@@ -1275,6 +1504,18 @@ void launch_prim_t(const Scene& sc, GeomState& g, float* dmeans, float* dconf, f
   cfg.numAttrs = l2_persist_attr(dtable, (size_t)sc.T * sc.L * F * sizeof(float), attr);
   cudaLaunchKernelEx(&cfg, k, sc, g, dmeans, dconf, dtable, dW);
   note_launches(1);
+  if (split) {
+    const size_t csmem = sizeof(float) * (corner_head_floats(D, sc.L, OMAX) + kCornerWarps * 32 * OMAX);
+    auto kc = backward_corner_kernel<F, OMAX>;
+    cudaFuncSetAttribute(kc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem);
+    cudaMemsetAsync(g.status + 8, 0, sizeof(uint32_t), s);
+    int cblocks = (sc.P + kCornerWarps - 1) / kCornerWarps;
+    const int cres = resident_blocks(reinterpret_cast<const void*>(kc), kCornerWarps * 32, csmem);
+    cblocks = cblocks < cres ? cblocks : cres;
+    if (cblocks < 1) cblocks = 1;
+    kc<<<cblocks, kCornerWarps * 32, csmem, s>>>(sc, g, dconf, dtable, dW);
+    note_launches(1);
+  }
 }
 
 // Properties of the records of primitives whose backward projection puts a
