@@ -1097,7 +1097,7 @@ __host__ __device__ inline int corner_head_floats(int D, int L, int OMAX) {
   return OMAX * bwd_dp(D) + 3 * pad4(L) + 8 * bwd_dp(D) + 3 * 8 * OMAX;
 }
 template <int F, int OMAX>
-__global__ void __launch_bounds__(kCornerWarps * 32) backward_corner_kernel(Scene sc, GeomState g,
+__global__ void __launch_bounds__(kCornerWarps * 32, OMAX == 8 ? 4 : 2) backward_corner_kernel(Scene sc, GeomState g,
                                                                              float* __restrict__ dconf,
                                                                              float* __restrict__ dtable,
                                                                              float* __restrict__ dW) {
@@ -1142,6 +1142,12 @@ __global__ void __launch_bounds__(kCornerWarps * 32) backward_corner_kernel(Scen
   const GridPt gpt = grid_point((int)lane < V ? (int)lane : 0, G, sc.gof);
   const bool act = (int)lane < V;
   constexpr int kGrab = 8;
+  // the next primitive's record pixels, confidences and centre are loaded while
+  // the current one is processed
+  int q_next = -1;
+  uint32_t rp_next = 0u;
+  float conf_next = 0.0f;
+  float3 c_next = make_float3(0.0f, 0.0f, 0.0f);
   for (;;) {
     int q0 = 0;
     if (lane == 0) q0 = (int)atomicAdd(g.status + 8, (unsigned)kGrab);
@@ -1158,11 +1164,27 @@ __global__ void __launch_bounds__(kCornerWarps * 32) backward_corner_kernel(Scen
       const int q = q0 + qi;
       const int cc = (int)(__shfl_sync(0xffffffffu, cbx, qi) & 7u);
       const size_t s0 = (size_t)q * V;
-      const uint32_t rp = act ? g.rec_pix[s0 + lane] : 0u;  // pixel + 1 of each grid point's record, else 0
-      const float conf = act ? sc.conf[s0 + lane] : 0.0f;
+      uint32_t rp;  // pixel + 1 of each grid point's record, else 0
+      float conf;
+      float3 c;
+      if (q_next == q) {
+        rp = rp_next;
+        conf = conf_next;
+        c = c_next;
+      } else {
+        rp = act ? g.rec_pix[s0 + lane] : 0u;
+        conf = act ? sc.conf[s0 + lane] : 0.0f;
+        c = make_float3(sc.means[3 * q], sc.means[3 * q + 1], sc.means[3 * q + 2]);
+      }
+      if (batch) {
+        q_next = q0 + __ffs(batch) - 1;
+        const size_t s1 = (size_t)q_next * V;
+        rp_next = act ? g.rec_pix[s1 + lane] : 0u;
+        conf_next = act ? sc.conf[s1 + lane] : 0.0f;
+        c_next = make_float3(sc.means[3 * q_next], sc.means[3 * q_next + 1], sc.means[3 * q_next + 2]);
+      }
       const uint32_t cm = __ballot_sync(0xffffffffu, rp != 0u);
       if (cm == 0) continue;
-      const float3 c = make_float3(sc.means[3 * q], sc.means[3 * q + 1], sc.means[3 * q + 2]);
       const float3 pos = grid_pos_rel(c, gpt.rel, sc.step);
       const float2 sb = project(pos, sc.proj, sc.W, sc.H, false);  // backward.cu:325
       const int bx = pix_coord(sb.x), by = pix_coord(sb.y);
