@@ -24,9 +24,13 @@
 //     per pixel and grid point; its features come from the feature stage's
 //     cache.  dW is reduced per CTA before global atomics; db = sum_p dpre_p is
 //     summed by the per-pixel pass, which writes every dpre_p once.
+//  3. backward_corner: the primitives whose grid points all clamp to one corner
+//     of the reference's fixed hashgrid box, which step 2 then skips: the same
+//     quantities with the box corner's features, without position classes.
 //
-// With the exact-gradient flag both kernels compute the derivative of the
-// forward instead (backward_pixel_exact_kernel, backward_prim_kernel<.., true>).
+// With the exact-gradient flag steps 1 and 2 compute the derivative of the
+// forward instead (backward_pixel_exact_kernel, backward_prim_kernel<.., true,
+// ..>), and step 2 takes every primitive.
 #include <cuda_runtime.h>
 
 #include <cstdint>
