@@ -281,3 +281,31 @@ def test_feature_stage_on_callers_table_layout(name, monkeypatch):
     monkeypatch.setenv("VI_TABLE_LAYOUT", "entry")
     means, conf, s = tl.custom_scene(seed=zlib.crc32(name.encode()) % 1000, **CUSTOM[name])
     _check(means, conf, s, seed=5)
+
+
+# Primitives spread over [-3, 3]^3 with the reference's fixed hashgrid box
+# [-1.3, 1.3]^3: about one in seven has every grid point clamped to one corner of
+# the box.  The backward hands those to backward_corner_kernel and the rest to
+# backward_prim_kernel; these cases run both across grid sizes, feature widths
+# and output widths (the benchmark scenes cover G = 3, F = 2 and 4, O = 8 only).
+CORNER = {
+    "corner_G3": dict(),
+    "corner_G2": dict(G=2),
+    "corner_G1": dict(G=1),
+    "corner_fout8_o12": dict(Fout=8),
+    "corner_F4L16_D64": dict(F=4, L=16),
+    "corner_F1L16": dict(F=1, L=16),
+    "corner_F8L4": dict(F=8, L=4),
+    "corner_K3": dict(K=3),
+}
+
+
+@pytest.mark.parametrize("name", sorted(CORNER))
+def test_box_corner_primitives(name):
+    kw = dict(P=600, extent=3.0, dist=9.0, scale=0.25, W=96, H=72)
+    kw.update(CORNER[name])
+    means, conf, s = tl.custom_scene(seed=zlib.crc32(name.encode()) % 1000, **kw)
+    # every grid point lies within scale/2 of the centre on each axis
+    clamped = (means.abs().cpu() > 1.3 + 0.5 * kw["scale"] + 1e-4).all(dim=1)
+    assert int(clamped.sum()) > 40
+    _check(means, conf, s, seed=11)
